@@ -1,0 +1,141 @@
+/*
+ * ptq8.h - C ABI of the B200-native (sm_100a) W8A8 / W4A8 quantized-conv engine.
+ *
+ * Drop-in boundary for the reference's int8 engine (PaperTigerL/ptq-int8-lab,
+ * 06-gpu-int8/cpp).  Each entry point names the reference interface it
+ * replaces.  Conventions: plain pointers and sizes; no entry point exits the
+ * process (the reference's CUDA_CHECK calls std::exit, int8_engine.cuh:109-117);
+ * every failure returns a nonzero status and the message is available from
+ * ptq8_engine_last_error() or the caller's err buffer.  The engine owns its
+ * device memory; the caller owns input / logits buffers and may provide the
+ * CUDA stream.  One engine per device per host thread.
+ */
+#ifndef PTQ8_H
+#define PTQ8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PTQ8_ABI_VERSION 1
+
+/* status codes */
+#define PTQ8_OK 0
+#define PTQ8_ERR_INVALID 1  /* bad argument / state / unsupported topology */
+#define PTQ8_ERR_FORMAT 2   /* malformed PTQ2 / PTQW / PTQC file */
+#define PTQ8_ERR_CUDA 3     /* CUDA runtime error */
+#define PTQ8_ERR_TIMEOUT 4  /* a bounded device wait ran out; outputs invalid */
+
+/* graph passes (ptq8_engine_build `passes` bit mask) */
+#define PTQ8_PASS_CENTER_TAP 1 /* 07-tensorrt-deploy/scripts/push_optimize_onnx.py:36-93 */
+#define PTQ8_PASS_DECOMPOSE 2  /* 07-tensorrt-deploy/scripts/push_decompose.py:99-202  */
+
+/* activation range modes (06-gpu-int8/cpp/ptq_quant.h:163) */
+#define PTQ8_ACT_ABSMAX 0
+#define PTQ8_ACT_MINMAX 1
+
+typedef struct ptq8_model ptq8_model;
+typedef struct ptq8_engine ptq8_engine;
+
+int ptq8_abi_version(void);
+
+/* ---- calibrated-model files ------------------------------------------------ */
+
+/* Model::load(path, err) - 06-gpu-int8/cpp/ptq_model.h:72-91.
+ * PTQW or PTQ2 by magic, strict EOF, topology validation (ptq_model.h:104-203).
+ * Returns NULL on failure with the reason in err. */
+ptq8_model* ptq8_model_load(const char* path, char* err, size_t errlen);
+void ptq8_model_free(ptq8_model* m);
+
+/* Counters of Model (ptq_model.h:65-70,205-229): out[11] = {n_conv, n_block,
+ * stem_pool, fc_in, fc_out, n_depthwise, n_grouped, n_relu6, n_residual2,
+ * format (1 PTQW, 2 PTQ2), convs per block}. */
+int ptq8_model_info(const ptq8_model* m, int* out);
+/* ConvSpec of conv i (ptq_model.h:46-55): {cout, cin, kh, kw, sh, sw, ph, pw, relu, groups}. */
+int ptq8_model_conv(const ptq8_model* m, int i, int* meta10);
+/* BlockSpec of block i (ptq_model.h:57-63). */
+int ptq8_model_block(const ptq8_model* m, int i, int* convs, int cap, int* n_convs, int* ds, int* stride,
+                     int* residual);
+/* Borrowed pointers to conv i's fp32 weight/bias (i = -1: the FC). */
+int ptq8_model_weights(const ptq8_model* m, int i, const float** weight, size_t* n_weight, const float** bias);
+
+/* load_ptqc(path, n_expected, out, err) - 06-gpu-int8/cpp/ptq_model.h:425-503.
+ * Writes n (lo, hi) pairs to lohi[2n] (cap = number of floats available). */
+int ptq8_load_ptqc(const char* path, size_t n_expected, float* lohi, size_t cap, char* err, size_t errlen);
+
+/* tensor_quant_from_range scale (ptq_quant.h:195-214), returned in float64 as the
+ * reference oracle uses it (09-ptq-toolkit/ptq_toolkit/ref_int8.py:69-87). */
+double ptq8_act_scale(float lo, float hi, int bits, int mode);
+/* quantize_weight_per_channel_sym (ptq_quant.h:72-110): w[cout][k] -> codes, f32 scales. */
+int ptq8_quantize_weight(const float* w, int cout, int k, int bits, int8_t* codes, float* scale32);
+
+/* ---- engine ---------------------------------------------------------------- */
+
+/* Int8Engine construction on CUDA device `device` (int8_engine.cuh:130). */
+ptq8_engine* ptq8_engine_create(int device);
+void ptq8_engine_destroy(ptq8_engine* e);
+const char* ptq8_engine_last_error(const ptq8_engine* e);
+
+/* Int8Engine::build(model, w_bits, a_bits) - int8_engine.cuh:132-349.
+ * layer_bits (nullable, n_layer_bits == n_conv): per-conv weight bits 8/4 from a
+ * layer plan (09-ptq-toolkit/ptq_toolkit/quant/mixed.py:126-212).  `passes` is a
+ * PTQ8_PASS_* mask applied to the quantized layers.  The model must outlive the
+ * engine (the reference keeps a raw pointer, int8_engine.cuh:134). */
+int ptq8_engine_build(ptq8_engine* e, const ptq8_model* m, int w_bits, int a_bits, const int* layer_bits,
+                      int n_layer_bits, int passes);
+/* Int8Engine::set_act_mode - int8_engine.cuh:353. */
+int ptq8_engine_set_act_mode(ptq8_engine* e, int mode);
+/* Int8Engine::set_calib(ranges) - int8_engine.cuh:362-406; lohi[2n]. */
+int ptq8_engine_set_calib(ptq8_engine* e, const float* lohi, size_t n);
+/* Network input geometry (default 3x32x32, ptq_model.h:104 validates with 32x32). */
+int ptq8_engine_set_input_shape(ptq8_engine* e, int c, int h, int w);
+/* Int8Engine::alloc_scratch(n) - int8_engine.cuh:807-833: plan the launches and
+ * allocate every activation buffer for batches up to max_batch. */
+int ptq8_engine_alloc_scratch(ptq8_engine* e, int max_batch);
+/* Int8Engine::set_stream - int8_engine.cuh:771 (NULL: engine-owned stream). */
+int ptq8_engine_set_stream(ptq8_engine* e, void* stream);
+void* ptq8_engine_stream(ptq8_engine* e);
+
+/* Int8Engine::forward(x_host, n, c, h, w, logits_host) - int8_engine.cuh:429-645.
+ * Host buffers: H2D, the whole forward as one CUDA graph, D2H, synchronize. */
+int ptq8_engine_forward(ptq8_engine* e, const float* x_host, int n, int c, int h, int w, float* logits_host);
+/* Device-pointer forward (fp32 NCHW input, fp32 [n][fc_out] logits); enqueued
+ * on the engine stream, not synchronized. */
+int ptq8_engine_forward_device(ptq8_engine* e, const float* x_dev, int n, float* logits_dev);
+/* Engine-resident buffers: callers may write inputs straight into the input
+ * buffer and run ptq8_engine_run() with no copies. */
+float* ptq8_engine_input_buffer(ptq8_engine* e);
+float* ptq8_engine_logits_buffer(ptq8_engine* e);
+int ptq8_engine_run(ptq8_engine* e, int n, int use_graph);
+/* Async device-to-device copy of the last forward's logits ([n][fc_out]) on the engine stream. */
+int ptq8_engine_copy_logits(ptq8_engine* e, int n, float* dst_dev);
+int ptq8_engine_sync(ptq8_engine* e);
+/* Reads and clears the device error word set by bounded waits. */
+int ptq8_engine_check_device_error(ptq8_engine* e);
+
+/* Parity dumps (replaces forward(..., stop_after_block, mid_out),
+ * int8_engine.cuh:429 and locate_block.cpp): what 0 = int8 input codes of conv
+ * `index` (NHWC, row pitch shape4[3]; the stem's are its im2col rows), what 1 =
+ * the fp32 map fed to the pooling head (NHWC).  shape4 = {N_max, H, W, ld}. */
+int ptq8_engine_tensor_info(ptq8_engine* e, int what, int index, int* shape4);
+int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst, size_t bytes);
+/* Per-launch timing (CUDA events on the engine stream, `iters` back-to-back
+ * launches of each step, not graph-captured) with each step's algorithmic work:
+ * ms[i], macs[i], bytes[i], kind[i] (0 stem im2col + GEMM, 1 tensor-core conv,
+ * 2 depthwise, 3 maxpool, 4 pooling head) for i < *n_steps (cap entries available).
+ * Replaces the reference's PROF_LAYERS per-conv events (int8_engine.cuh:168-176,901-931). */
+int ptq8_engine_profile(ptq8_engine* e, int n, int iters, float* ms, double* macs, double* bytes, int* kind,
+                        int cap, int* n_steps);
+/* Number of kernel launches in one forward (the CUDA graph's kernel nodes). */
+int ptq8_engine_n_launches(const ptq8_engine* e);
+/* Human-readable record of what the graph passes did. */
+int ptq8_engine_passes_log(const ptq8_engine* e, char* out, size_t cap);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PTQ8_H */

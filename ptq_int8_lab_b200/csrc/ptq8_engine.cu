@@ -1,0 +1,1166 @@
+// Int8 engine: topology interpreter, device buffers, TMA descriptors, CUDA
+// graph replay, and the extern "C" boundary declared in include/ptq8.h.
+//
+// Execution model (mirrors Int8Engine::forward, 06-gpu-int8/cpp/int8_engine.cuh:429-645,
+// and the topology semantics of 09-.../export/topoblocks.py:181-220):
+//   stem conv [-> maxpool] -> blocks (ds conv first, then the block's convs;
+//   the residual add + post activation run in the last conv's epilogue) ->
+//   global average pool + FC.
+// Every intermediate is a separate device buffer (no aliasing), so any conv's
+// input codes can be dumped after a forward for bit-exact parity checks.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "ptq8_kernels.cuh"
+#include "ptq8_model.hpp"
+#include "../../include/ptq8.h"
+
+using namespace ptq8;
+
+namespace {
+
+constexpr int kStages = 4;
+
+std::string strf(const char* f, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, f);
+    std::vsnprintf(buf, sizeof buf, f, ap);
+    va_end(ap);
+    return buf;
+}
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+CUtensorMapSwizzle swizzle_for(int cb) {
+    return cb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (cb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+// An fp32 activation of the network and the int8 code tensors made from it.
+struct Value {
+    int h = 0, w = 0, c = 0;   // per-image NHWC shape
+    bool need_f32 = false;
+    std::vector<double> scales;  // distinct consumer scales, in first-use order
+    int ldq = 0;                 // code row pitch (c rounded up to 32)
+    float* f32 = nullptr;
+    std::vector<int8_t*> codes;  // one per scale
+    int code_index(double s) const {
+        for (size_t i = 0; i < scales.size(); ++i)
+            if (scales[i] == s) return (int)i;
+        return -1;
+    }
+};
+
+enum LaunchKind { K_STEM_IM2COL = 0, K_TC = 1, K_DW = 2, K_MAXPOOL = 3 };
+
+struct Step {
+    int kind = K_TC;
+    int conv = -1;        // model conv index (or -1 for maxpool)
+    int in_val = -1;      // value read (codes at conv scale; fp32 for maxpool)
+    int out_val = -1;     // value produced
+    int res_val = -1;     // residual value (fp32), -1 none
+    int post = 0;         // 0 none, 1 add + relu, 2 add
+    int act = 0;
+    // geometry
+    int ih = 0, iw = 0, ic = 0, oh = 0, ow = 0, oc = 0;
+    int kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0;
+    int cb = 32, bn = 16, n_ntiles = 1, ktot = 0, kpad = 0;
+    int TW = 1, TH = 1, TN = 1;
+    double s_in = 1.0;
+    // device parameters
+    int8_t* d_w = nullptr;
+    float* d_factor = nullptr;
+    float* d_bias = nullptr;
+    int8_t* d_im2col = nullptr;   // stem rows
+    CUtensorMap map_a{}, map_b{};
+};
+
+struct ConvQ {   // quantized conv after graph passes
+    ConvSpec spec;              // geometry (weight field unused)
+    int bits = 8;
+    std::vector<int8_t> codes;  // [cout][cin*kh*kw] in (c,i,j) order
+    std::vector<float> wscale;  // [cout]
+    std::vector<float> bias;
+    // positional decomposition: output channel c' = pos*cout_orig + c (NHWC == D2S DCR)
+    int view_oh = 0, view_ow = 0;   // >0 when the conv runs as a 1x1-output GEMM
+};
+
+}  // namespace
+
+struct ptq8_model {
+    Model m;
+};
+
+struct ptq8_engine {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    std::string err;
+    const Model* model = nullptr;   // caller keeps the model alive (int8_engine.cuh:134)
+    int w_bits = 8, a_bits = 8, act_mode = ACT_ABSMAX, passes = 0;
+    std::vector<int> layer_bits;
+    std::vector<ConvQ> q;
+    std::vector<std::pair<float, float>> ranges;
+    std::vector<double> scale;     // per conv input scale (double)
+    bool built = false, calibrated = false, planned = false;
+    int in_c = 3, in_h = 32, in_w = 32;
+    int max_batch = 0;
+    // plan
+    std::vector<Value> vals;
+    std::vector<Step> steps;
+    int final_val = -1;
+    std::vector<int> conv_step;    // conv index -> step index
+    float* d_input = nullptr;      // fp32 NCHW [max_batch][3][32][32]
+    float* d_logits = nullptr;
+    float* d_fc_w = nullptr;
+    float* d_fc_b = nullptr;
+    std::vector<void*> allocs;
+    std::map<int, cudaGraphExec_t> graphs;
+    std::vector<std::string> passes_log;
+
+    ~ptq8_engine() { release(); }
+
+    void release() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        graphs.clear();
+        for (void* p : allocs) cudaFree(p);
+        allocs.clear();
+        if (own_stream && stream) cudaStreamDestroy(stream);
+        stream = nullptr;
+        own_stream = false;
+    }
+
+    int fail(const std::string& m, int code = PTQ8_ERR_INVALID) {
+        err = m;
+        return code;
+    }
+
+    bool cuda_ok(cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return true;
+        err = strf("%s: %s", what, cudaGetErrorString(e));
+        return false;
+    }
+
+    template <class T>
+    bool dalloc(T** p, size_t bytes, const char* what) {
+        void* v = nullptr;
+        if (!cuda_ok(cudaMalloc(&v, bytes ? bytes : 16), what)) return false;
+        allocs.push_back(v);
+        *p = reinterpret_cast<T*>(v);
+        return true;
+    }
+};
+
+namespace {
+
+// ------------------------------------------------------------------ graph passes
+
+// Center tap (07-tensorrt-deploy/scripts/push_optimize_onnx.py:36-93): a kxk conv
+// (k odd, stride 1, pad (k-1)/2) whose input and output maps are 1x1 only ever
+// multiplies the center tap by real data; the others see padding code 0.  The
+// rewrite keeps the int8 codes of the center tap and the per-channel scales of
+// the full kernel, so the int32 accumulators are unchanged.
+bool center_tap(ConvQ& cq, int ih, int iw, std::string* note) {
+    ConvSpec& c = cq.spec;
+    if (ih != 1 || iw != 1 || c.kh != c.kw || c.kh % 2 == 0 || c.kh == 1) return false;
+    if (c.sh != 1 || c.sw != 1 || c.ph != c.kh / 2 || c.pw != c.kw / 2 || c.groups != 1) return false;
+    const int k = c.kh, ctr = k / 2, cin = c.cin;
+    std::vector<int8_t> nc((size_t)c.cout * cin);
+    for (int o = 0; o < c.cout; ++o)
+        for (int ci = 0; ci < cin; ++ci)
+            nc[(size_t)o * cin + ci] = cq.codes[(((size_t)o * cin + ci) * k + ctr) * k + ctr];
+    cq.codes.swap(nc);
+    c.kh = c.kw = 1;
+    c.ph = c.pw = 0;
+    *note = strf("center-tap %dx%d -> 1x1", k, k);
+    return true;
+}
+
+// One spatial dimension of the positional decomposition
+// (07-tensorrt-deploy/scripts/push_decompose.py:50-80): per output position the
+// valid kernel slice; uniform when every position reads the whole input with
+// the same number of taps.
+bool uniform_dim(int H, int k, int p, int s, int* OH, int* t, std::vector<int>* los) {
+    *OH = (H + 2 * p - k) / s + 1;
+    los->clear();
+    int tt = -1;
+    for (int i = 0; i < *OH; ++i) {
+        const int lo = std::max(0, p - s * i);
+        const int hi = std::min(k - 1, H - 1 + p - s * i);
+        if (lo > hi) return false;
+        const int r_lo = s * i - p + lo, r_hi = s * i - p + hi;
+        if (r_lo != 0 || r_hi != H - 1) return false;
+        if (tt < 0) tt = hi - lo + 1;
+        if (hi - lo + 1 != tt) return false;
+        los->push_back(lo);
+    }
+    *t = tt;
+    return true;
+}
+
+// Positional decomposition (push_decompose.py:99-202): a conv whose input map is
+// no larger than its kernel becomes one th x tw conv with OH*OW*cout outputs
+// (position-major weight blocks, tiled bias) followed by DepthToSpace(DCR).
+// In NHWC memory the DCR rearrangement is the identity: output channel
+// (i*OW+j)*cout + c of image n is element (n, i, j, c).  Codes and scales are
+// sliced from the quantized kernel, so the accumulators are unchanged.
+bool decompose(ConvQ& cq, int H, int W, std::string* note) {
+    ConvSpec& c = cq.spec;
+    if (c.groups != 1 || c.kh != c.kw || c.kh % 2 == 0) return false;
+    const int k = c.kh, p = (k - 1) / 2;
+    if (c.ph != p || c.pw != p) return false;
+    if (H > k || W > k) return false;
+    int OH, OW, th, tw;
+    std::vector<int> lh, lw;
+    if (!uniform_dim(H, k, p, c.sh, &OH, &th, &lh) || !uniform_dim(W, k, p, c.sw, &OW, &tw, &lw)) return false;
+    if (th == k && tw == k && p == 0) return false;
+    if (OH > 1 && OH != OW) return false;
+    // NHWC identity of the DCR rearrangement needs the code rows unpadded
+    if ((OH > 1 || OW > 1) && c.cout % 32 != 0) return false;
+    const int cout = c.cout, cin = c.cin;
+    const int ncout = OH * OW * cout;
+    std::vector<int8_t> nc((size_t)ncout * cin * th * tw);
+    std::vector<float> ns((size_t)ncout), nb((size_t)ncout);
+    for (int i = 0; i < OH; ++i)
+        for (int j = 0; j < OW; ++j) {
+            const int blk = (i * OW + j) * cout;
+            for (int o = 0; o < cout; ++o) {
+                ns[blk + o] = cq.wscale[o];
+                nb[blk + o] = cq.bias[o];
+                for (int ci = 0; ci < cin; ++ci)
+                    for (int a = 0; a < th; ++a)
+                        for (int b = 0; b < tw; ++b)
+                            nc[(((size_t)(blk + o) * cin + ci) * th + a) * tw + b] =
+                                cq.codes[(((size_t)o * cin + ci) * k + lh[i] + a) * k + lw[j] + b];
+            }
+        }
+    *note = strf("decompose %dx%d s%d on %dx%d -> %dx%d conv, %d outputs%s", k, k, c.sh, H, W, th, tw, ncout,
+                 (OH > 1 || OW > 1) ? strf(" + DepthToSpace(%d)", OH).c_str() : "");
+    cq.codes.swap(nc);
+    cq.wscale.swap(ns);
+    cq.bias.swap(nb);
+    cq.view_oh = OH;
+    cq.view_ow = OW;
+    c.kh = th;
+    c.kw = tw;
+    c.sh = c.sw = 1;
+    c.ph = c.pw = 0;
+    return true;
+}
+
+// ------------------------------------------------------------------ planning
+
+int new_value(ptq8_engine* e, int h, int w, int c) {
+    Value v;
+    v.h = h;
+    v.w = w;
+    v.c = c;
+    v.ldq = round_up(c, 32);
+    e->vals.push_back(v);
+    return (int)e->vals.size() - 1;
+}
+
+void need_codes(ptq8_engine* e, int val, double s) {
+    Value& v = e->vals[val];
+    if (v.code_index(s) < 0) v.scales.push_back(s);
+}
+
+void tile_shape(int N, int OH, int OW, int* TW, int* TH, int* TN) {
+    if (OW >= 128) {
+        *TW = 128; *TH = 1; *TN = 1;
+        return;
+    }
+    *TW = OW;
+    *TH = std::max(1, std::min(OH, 128 / OW));
+    *TN = std::max(1, std::min(128 / (OW * *TH), 256));
+    (void)N;
+}
+
+int choose_cb(int cpad) { return cpad % 128 == 0 ? 128 : (cpad % 64 == 0 ? 64 : 32); }
+
+void choose_bn(int cout, int* bn, int* ntiles) {
+    const int nt = (cout + 255) / 256;
+    *ntiles = nt;
+    *bn = round_up((cout + nt - 1) / nt, 16);
+}
+
+int plan(ptq8_engine* e) {
+    const Model& m = *e->model;
+    e->vals.clear();
+    e->steps.clear();
+    e->conv_step.assign(m.convs.size(), -1);
+    e->passes_log.clear();
+
+    // --- shapes of every conv input, computed along the topology
+    std::vector<int> in_h(m.convs.size(), 0), in_w(m.convs.size(), 0);
+    auto add_conv = [&](int ci, int in_val, int* out_val, int res_val, int post) -> int {
+        const Value& vin = e->vals[in_val];
+        ConvQ& cq = e->q[ci];
+        const ConvSpec& c = cq.spec;
+        Step st;
+        st.conv = ci;
+        st.in_val = in_val;
+        st.ih = vin.h;
+        st.iw = vin.w;
+        st.ic = c.in_channels();
+        st.kh = c.kh; st.kw = c.kw; st.sh = c.sh; st.sw = c.sw; st.ph = c.ph; st.pw = c.pw;
+        st.act = c.relu;
+        st.s_in = e->scale[ci];
+        int oh = conv_out_dim(vin.h, c.kh, c.sh, c.ph), ow = conv_out_dim(vin.w, c.kw, c.sw, c.pw);
+        int oc = c.cout;
+        if (cq.view_oh > 0) {   // decomposed conv: outputs as (view_oh, view_ow, cout/(view_oh*view_ow))
+            oc = c.cout / (cq.view_oh * cq.view_ow);
+            st.oh = 1; st.ow = 1;
+        } else {
+            st.oh = oh; st.ow = ow;
+        }
+        const int vh = cq.view_oh > 0 ? cq.view_oh : oh, vw = cq.view_ow > 0 ? cq.view_ow : ow;
+        st.oc = c.cout;
+        *out_val = new_value(e, vh, vw, oc);
+        st.out_val = *out_val;
+        st.res_val = res_val;
+        st.post = post;
+        if (c.depthwise()) {
+            st.kind = K_DW;
+        } else if (c.groups != 1) {
+            return e->fail(strf("conv[%d]: grouped conv with groups=%d (not depthwise) is not supported", ci, c.groups));
+        } else {
+            st.kind = K_TC;
+        }
+        if (e->vals[in_val].f32 == nullptr && in_val == 0 && ci == 0) st.kind = K_STEM_IM2COL;
+        if (st.kind != K_STEM_IM2COL) need_codes(e, in_val, e->scale[ci]);
+        e->conv_step[ci] = (int)e->steps.size();
+        e->steps.push_back(st);
+        return PTQ8_OK;
+    };
+
+    // value 0: network input (fp32 NCHW, read by the stem im2col kernel)
+    new_value(e, e->in_h, e->in_w, e->in_c);
+    int cur = -1;
+    int rc = add_conv(0, 0, &cur, -1, 0);
+    if (rc) return rc;
+    if (m.stem_pool) {
+        Value& v0 = e->vals[cur];
+        v0.need_f32 = true;
+        const int ph = (v0.h + 2 - 3) / 2 + 1, pw = (v0.w + 2 - 3) / 2 + 1;
+        const int pv = new_value(e, ph, pw, v0.c);
+        Step st;
+        st.kind = K_MAXPOOL;
+        st.in_val = cur;
+        st.out_val = pv;
+        st.ih = e->vals[cur].h; st.iw = e->vals[cur].w; st.ic = e->vals[cur].c;
+        st.oh = ph; st.ow = pw; st.oc = e->vals[cur].c;
+        e->steps.push_back(st);
+        cur = pv;
+    }
+    for (size_t bi = 0; bi < m.blocks.size(); ++bi) {
+        const BlockSpec& b = m.blocks[bi];
+        std::vector<int> cs;
+        for (int ci : b.convs)
+            if (ci >= 0) cs.push_back(ci);
+        int ident = -1;
+        if (b.residual != 0) {
+            if (b.ds >= 0) {
+                int dv;
+                rc = add_conv(b.ds, cur, &dv, -1, 0);
+                if (rc) return rc;
+                ident = dv;
+            } else {
+                ident = cur;
+            }
+            e->vals[ident].need_f32 = true;
+        }
+        int t = cur;
+        for (size_t k = 0; k < cs.size(); ++k) {
+            const bool last = k + 1 == cs.size();
+            int ov;
+            rc = add_conv(cs[k], t, &ov, last && b.residual ? ident : -1, last ? b.residual : 0);
+            if (rc) return rc;
+            t = ov;
+        }
+        cur = t;
+    }
+    e->vals[cur].need_f32 = true;
+    e->final_val = cur;
+    const Value& fv = e->vals[cur];
+    if (fv.c != m.fc_in) return e->fail(strf("final map has %d channels but fc_in=%d", fv.c, m.fc_in));
+    for (Value& v : e->vals)
+        if (v.scales.size() > 2)
+            return e->fail("a tensor feeds more than two distinct activation scales (unsupported)");
+    return PTQ8_OK;
+}
+
+bool make_map(ptq8_engine* e, CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base, const cuuint64_t* dims,
+              const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* estr, CUtensorMapSwizzle swz) {
+    auto enc = get_encode();
+    if (!enc) {
+        e->err = "cuTensorMapEncodeTiled entry point not available";
+        return false;
+    }
+    CUresult r = enc(map, dt, rank, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        e->err = strf("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return false;
+    }
+    return true;
+}
+
+size_t conv_smem_bytes(int cb, int bn) {
+    return (size_t)kStages * (128 * cb + round_up(bn * cb, 1024)) + 1024 + 8 * (2 * kStages + 1) + 16 + 2 * 4 * round_up(bn, 32) + 64;
+}
+
+int finalize(ptq8_engine* e, int max_batch) {
+    const Model& m = *e->model;
+    if (!e->built) return e->fail("engine not built");
+    if (!e->calibrated) return e->fail("calibration ranges not set (set_calib)");
+    if (max_batch <= 0) return e->fail("max_batch must be positive");
+    if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+    for (void* p : e->allocs) cudaFree(p);
+    e->allocs.clear();
+    e->planned = false;
+    int rc = plan(e);
+    if (rc) return rc;
+    const size_t NB = (size_t)max_batch;
+
+    // activation buffers
+    for (size_t vi = 0; vi < e->vals.size(); ++vi) {
+        Value& v = e->vals[vi];
+        const size_t pix = NB * v.h * v.w;
+        v.codes.assign(v.scales.size(), nullptr);
+        if (vi == 0) continue;   // network input lives in d_input
+        if (v.need_f32 && !e->dalloc(&v.f32, pix * v.c * sizeof(float), "alloc fp32 activation")) return PTQ8_ERR_CUDA;
+        for (size_t k = 0; k < v.scales.size(); ++k)
+            if (!e->dalloc(&v.codes[k], pix * v.ldq, "alloc int8 codes")) return PTQ8_ERR_CUDA;
+    }
+    if (!e->dalloc(&e->d_input, NB * e->in_c * e->in_h * e->in_w * sizeof(float), "alloc input")) return PTQ8_ERR_CUDA;
+    if (!e->dalloc(&e->d_logits, NB * m.fc_out * sizeof(float), "alloc logits")) return PTQ8_ERR_CUDA;
+    if (!e->dalloc(&e->d_fc_w, m.fc_w.size() * sizeof(float), "alloc fc") ||
+        !e->dalloc(&e->d_fc_b, m.fc_b.size() * sizeof(float), "alloc fc"))
+        return PTQ8_ERR_CUDA;
+    cudaMemcpy(e->d_fc_w, m.fc_w.data(), m.fc_w.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(e->d_fc_b, m.fc_b.data(), m.fc_b.size() * 4, cudaMemcpyHostToDevice);
+
+    // per-step weights, epilogue constants and tensor maps
+    for (Step& st : e->steps) {
+        if (st.kind == K_MAXPOOL) continue;
+        const ConvQ& cq = e->q[st.conv];
+        const ConvSpec& c = cq.spec;
+        std::vector<float> factor(c.cout);
+        const float s32 = (float)st.s_in;
+        for (int o = 0; o < c.cout; ++o) factor[o] = s32 * cq.wscale[o];
+        if (!e->dalloc(&st.d_factor, c.cout * 4, "alloc factor") || !e->dalloc(&st.d_bias, c.cout * 4, "alloc bias"))
+            return PTQ8_ERR_CUDA;
+        cudaMemcpy(st.d_factor, factor.data(), c.cout * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(st.d_bias, cq.bias.data(), c.cout * 4, cudaMemcpyHostToDevice);
+        const int K = c.cin * c.kh * c.kw;
+        if (st.kind == K_DW) {
+            std::vector<int8_t> w((size_t)c.kh * c.kw * c.cout);
+            for (int o = 0; o < c.cout; ++o)
+                for (int t = 0; t < c.kh * c.kw; ++t) w[(size_t)t * c.cout + o] = cq.codes[(size_t)o * K + t];
+            if (!e->dalloc(&st.d_w, w.size(), "alloc dw weights")) return PTQ8_ERR_CUDA;
+            cudaMemcpy(st.d_w, w.data(), w.size(), cudaMemcpyHostToDevice);
+            continue;
+        }
+        // tensor-core conv: weight matrix [cout][ktot] int8, K-major
+        std::vector<int8_t> w;
+        int cpad;
+        if (st.kind == K_STEM_IM2COL) {
+            st.kpad = round_up(K, 32);
+            cpad = st.kpad;
+            st.ktot = st.kpad;
+            w.assign((size_t)c.cout * st.ktot, 0);
+            for (int o = 0; o < c.cout; ++o)
+                for (int ci = 0; ci < c.cin; ++ci)
+                    for (int i = 0; i < c.kh; ++i)
+                        for (int j = 0; j < c.kw; ++j)
+                            w[(size_t)o * st.ktot + (i * c.kw + j) * c.cin + ci] =
+                                cq.codes[(((size_t)o * c.cin + ci) * c.kh + i) * c.kw + j];
+            if (!e->dalloc(&st.d_im2col, NB * st.oh * st.ow * st.kpad, "alloc im2col")) return PTQ8_ERR_CUDA;
+        } else {
+            cpad = round_up(c.cin, 32);
+            st.ktot = c.kh * c.kw * cpad;
+            w.assign((size_t)c.cout * st.ktot, 0);
+            for (int o = 0; o < c.cout; ++o)
+                for (int ci = 0; ci < c.cin; ++ci)
+                    for (int i = 0; i < c.kh; ++i)
+                        for (int j = 0; j < c.kw; ++j)
+                            w[(size_t)o * st.ktot + (i * c.kw + j) * cpad + ci] =
+                                cq.codes[(((size_t)o * c.cin + ci) * c.kh + i) * c.kw + j];
+        }
+        st.cb = choose_cb(cpad);
+        choose_bn(c.cout, &st.bn, &st.n_ntiles);
+        if (!e->dalloc(&st.d_w, w.size(), "alloc weights")) return PTQ8_ERR_CUDA;
+        cudaMemcpy(st.d_w, w.data(), w.size(), cudaMemcpyHostToDevice);
+        {
+            cuuint64_t dims[2] = {(cuuint64_t)st.ktot, (cuuint64_t)c.cout};
+            cuuint64_t strides[1] = {(cuuint64_t)st.ktot};
+            cuuint32_t box[2] = {(cuuint32_t)st.cb, (cuuint32_t)st.bn};
+            cuuint32_t estr[2] = {1, 1};
+            if (!make_map(e, &st.map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, st.d_w, dims, strides, box, estr,
+                          swizzle_for(st.cb)))
+                return PTQ8_ERR_CUDA;
+        }
+        tile_shape(max_batch, st.oh, st.ow, &st.TW, &st.TH, &st.TN);
+        if (st.kind == K_STEM_IM2COL) {
+            // the im2col rows form a [N][OH][OW][kpad] map read as a 1x1 conv
+            cuuint64_t dims[4] = {(cuuint64_t)st.kpad, (cuuint64_t)st.ow, (cuuint64_t)st.oh, (cuuint64_t)max_batch};
+            cuuint64_t strides[3] = {(cuuint64_t)st.kpad, (cuuint64_t)st.kpad * st.ow,
+                                     (cuuint64_t)st.kpad * st.ow * st.oh};
+            cuuint32_t box[4] = {(cuuint32_t)st.cb, (cuuint32_t)st.TW, (cuuint32_t)st.TH, (cuuint32_t)st.TN};
+            cuuint32_t estr[4] = {1, 1, 1, 1};
+            if (!make_map(e, &st.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, st.d_im2col, dims, strides, box, estr,
+                          swizzle_for(st.cb)))
+                return PTQ8_ERR_CUDA;
+        } else {
+            const Value& vin = e->vals[st.in_val];
+            int8_t* base = vin.codes[vin.code_index(st.s_in)];
+            cuuint64_t dims[4] = {(cuuint64_t)vin.c, (cuuint64_t)vin.w, (cuuint64_t)vin.h, (cuuint64_t)max_batch};
+            cuuint64_t strides[3] = {(cuuint64_t)vin.ldq, (cuuint64_t)vin.ldq * vin.w, (cuuint64_t)vin.ldq * vin.w * vin.h};
+            cuuint32_t box[4] = {(cuuint32_t)st.cb, (cuuint32_t)(st.TW * st.sw), (cuuint32_t)(st.TH * st.sh),
+                                 (cuuint32_t)st.TN};
+            cuuint32_t estr[4] = {1, (cuuint32_t)st.sw, (cuuint32_t)st.sh, 1};
+            if (box[1] > 256 || box[2] > 256 || st.sw > 8 || st.sh > 8)
+                return e->fail(strf("conv[%d]: tile/stride outside the TMA box limits", st.conv));
+            if (!make_map(e, &st.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, box, estr,
+                          swizzle_for(st.cb)))
+                return PTQ8_ERR_CUDA;
+        }
+    }
+    {
+        const int mx = (int)conv_smem_bytes(128, 256);
+        if (!e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<32, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr") ||
+            !e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<64, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr") ||
+            !e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<128, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr"))
+            return PTQ8_ERR_CUDA;
+    }
+    if (!e->stream) {
+        if (!e->cuda_ok(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) return PTQ8_ERR_CUDA;
+        e->own_stream = true;
+    }
+    e->max_batch = max_batch;
+    e->planned = true;
+    return PTQ8_OK;
+}
+
+EpiParams epi_for(ptq8_engine* e, const Step& st) {
+    EpiParams p{};
+    const Value& out = e->vals[st.out_val];
+    p.factor = st.d_factor;
+    p.bias = st.d_bias;
+    p.residual = st.res_val >= 0 ? e->vals[st.res_val].f32 : nullptr;
+    p.out_f32 = out.need_f32 ? out.f32 : nullptr;
+    p.cout = st.kind == K_MAXPOOL ? out.c : st.oc;
+    p.act = st.act;
+    p.post = st.res_val >= 0 ? st.post : 0;
+    p.out_q0 = out.codes.size() > 0 ? out.codes[0] : nullptr;
+    p.out_q1 = out.codes.size() > 1 ? out.codes[1] : nullptr;
+    p.ldq0 = p.ldq1 = out.ldq;
+    if (out.scales.size() > 0) { p.s0 = out.scales[0]; p.inv0 = (float)(1.0 / out.scales[0]); }
+    if (out.scales.size() > 1) { p.s1 = out.scales[1]; p.inv1 = (float)(1.0 / out.scales[1]); }
+    return p;
+}
+
+// Launch step `si` (si == steps.size(): the pooling head) for batch n on the engine stream.
+void enqueue_step(ptq8_engine* e, int n, size_t si) {
+    cudaStream_t s = e->stream;
+    if (si == e->steps.size()) {
+        const Value& fv = e->vals[e->final_val];
+        const Model& m = *e->model;
+        head_kernel<<<n, 256, fv.c * sizeof(float), s>>>(fv.f32, fv.h * fv.w, fv.c, e->d_fc_w, e->d_fc_b, m.fc_out,
+                                                         e->d_logits);
+        return;
+    }
+    const Step& st = e->steps[si];
+    EpiParams ep = epi_for(e, st);
+    if (st.kind == K_MAXPOOL) {
+        const size_t total = (size_t)n * st.oh * st.ow * st.oc;
+        const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 32);
+        maxpool_kernel<<<grid, 256, 0, s>>>(e->vals[st.in_val].f32, n, st.ih, st.iw, st.ic, st.oh, st.ow, ep);
+        return;
+    }
+    if (st.kind == K_DW) {
+        const Value& vin = e->vals[st.in_val];
+        const int8_t* in = vin.codes[vin.code_index(st.s_in)];
+        const size_t total = (size_t)n * st.oh * st.ow * ((st.oc + 3) / 4);
+        const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 64);
+        dw_conv_kernel<<<grid, 256, 0, s>>>(in, vin.ldq, st.d_w, n, st.ih, st.iw, st.oc, st.oh, st.ow, st.kh,
+                                            st.kw, st.sh, st.sw, st.ph, st.pw, ep);
+        return;
+    }
+    if (st.kind == K_STEM_IM2COL) {
+        const ConvSpec& c = e->q[st.conv].spec;
+        const size_t words = (size_t)n * st.oh * st.ow * (st.kpad / 4);
+        const int grid = (int)std::min<size_t>((words + 255) / 256, 148 * 64);
+        stem_im2col_kernel<<<grid, 256, 0, s>>>(e->d_input, st.d_im2col, n, c.cin, st.ih, st.iw, st.oh, st.ow,
+                                                c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad,
+                                                (float)(1.0 / st.s_in), st.s_in);
+    }
+    ConvGeom g{};
+    g.N = n;
+    g.OH = st.oh;
+    g.OW = st.ow;
+    g.TW = st.TW; g.TH = st.TH; g.TN = st.TN;
+    g.tiles_w = (st.ow + st.TW - 1) / st.TW;
+    g.tiles_h = (st.oh + st.TH - 1) / st.TH;
+    const int tiles_n = (n + st.TN - 1) / st.TN;
+    if (st.kind == K_STEM_IM2COL) {
+        g.KW = 1; g.SH = 1; g.SW = 1; g.PH = 0; g.PW = 0;
+        g.n_cchunks = st.kpad / st.cb;
+        g.n_kchunks = g.n_cchunks;
+    } else {
+        g.KW = st.kw; g.SH = st.sh; g.SW = st.sw; g.PH = st.ph; g.PW = st.pw;
+        g.n_cchunks = e->vals[st.in_val].ldq / st.cb;
+        g.n_kchunks = st.kh * st.kw * g.n_cchunks;
+    }
+    g.BN = st.bn;
+    int tc = 32;
+    while (tc < st.bn) tc <<= 1;
+    g.tmem_cols = tc;
+    g.a_bytes = (uint32_t)(st.TW * st.TH * st.TN * st.cb);
+    g.b_bytes = (uint32_t)(st.bn * st.cb);
+    dim3 grid((unsigned)(g.tiles_w * g.tiles_h * tiles_n), (unsigned)st.n_ntiles);
+    const size_t smem = conv_smem_bytes(st.cb, st.bn);
+    if (st.cb == 128)
+        conv_tc_kernel<128, kStages><<<grid, kConvThreads, smem, s>>>(st.map_a, st.map_b, g, ep);
+    else if (st.cb == 64)
+        conv_tc_kernel<64, kStages><<<grid, kConvThreads, smem, s>>>(st.map_a, st.map_b, g, ep);
+    else
+        conv_tc_kernel<32, kStages><<<grid, kConvThreads, smem, s>>>(st.map_a, st.map_b, g, ep);
+}
+
+int enqueue(ptq8_engine* e, int n) {
+    for (size_t si = 0; si <= e->steps.size(); ++si) enqueue_step(e, n, si);
+    if (!e->cuda_ok(cudaGetLastError(), "kernel launch")) return PTQ8_ERR_CUDA;
+    return PTQ8_OK;
+}
+
+// Algorithmic work of step si for batch n: multiply-accumulates and the bytes a
+// perfect kernel moves (input codes once, weights once, every output once).
+void step_work(const ptq8_engine* e, int n, size_t si, double* macs, double* bytes, int* kind) {
+    if (si == e->steps.size()) {
+        const Value& fv = e->vals[e->final_val];
+        *kind = 4;
+        *macs = (double)n * e->model->fc_in * e->model->fc_out;
+        *bytes = (double)n * fv.h * fv.w * fv.c * 4.0 + (double)n * e->model->fc_out * 4.0;
+        return;
+    }
+    const Step& st = e->steps[si];
+    const Value& out = e->vals[st.out_val];
+    double outb = (double)n * out.h * out.w * out.c * ((out.need_f32 ? 4.0 : 0.0) + (double)out.scales.size());
+    double resb = st.res_val >= 0 ? (double)n * out.h * out.w * out.c * 4.0 : 0.0;
+    *kind = st.kind;
+    if (st.kind == K_MAXPOOL) {
+        *macs = 0;
+        *bytes = (double)n * st.ih * st.iw * st.ic * 4.0 + outb;
+        return;
+    }
+    const ConvSpec& c = e->q[st.conv].spec;
+    const double pos = (double)n * st.oh * st.ow;
+    *macs = pos * c.cout * (double)c.cin * c.kh * c.kw;
+    const double inb = st.kind == K_STEM_IM2COL ? (double)n * st.ih * st.iw * st.ic * 4.0
+                                                : (double)n * st.ih * st.iw * st.ic;
+    *bytes = inb + (double)c.cout * c.cin * c.kh * c.kw + outb + resb;
+}
+
+int launch(ptq8_engine* e, int n, bool use_graph) {
+    if (!e->planned) {
+        int rc = finalize(e, std::max(n, e->max_batch > 0 ? e->max_batch : n));
+        if (rc) return rc;
+    }
+    if (n <= 0 || n > e->max_batch)
+        return e->fail(strf("batch %d outside [1, %d] (alloc_scratch sets the maximum)", n, e->max_batch));
+    if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
+    if (!use_graph) return enqueue(e, n);
+    auto it = e->graphs.find(n);
+    if (it == e->graphs.end()) {
+        cudaGraph_t g;
+        if (!e->cuda_ok(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture"))
+            return PTQ8_ERR_CUDA;
+        int rc = enqueue(e, n);
+        cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+        if (rc) return rc;
+        if (!e->cuda_ok(ce, "end capture")) return PTQ8_ERR_CUDA;
+        cudaGraphExec_t ge;
+        ce = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        if (!e->cuda_ok(ce, "graph instantiate")) return PTQ8_ERR_CUDA;
+        it = e->graphs.emplace(n, ge).first;
+    }
+    if (!e->cuda_ok(cudaGraphLaunch(it->second, e->stream), "graph launch")) return PTQ8_ERR_CUDA;
+    return PTQ8_OK;
+}
+
+void copy_err(const std::string& m, char* err, size_t errlen) {
+    if (err && errlen) {
+        std::snprintf(err, errlen, "%s", m.c_str());
+    }
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+
+extern "C" {
+
+int ptq8_abi_version(void) { return PTQ8_ABI_VERSION; }
+
+ptq8_model* ptq8_model_load(const char* path, char* err, size_t errlen) {
+    if (!path) {
+        copy_err("null path", err, errlen);
+        return nullptr;
+    }
+    auto* m = new ptq8_model();
+    std::string e;
+    if (!m->m.load(path, &e)) {
+        copy_err(e, err, errlen);
+        delete m;
+        return nullptr;
+    }
+    copy_err("", err, errlen);
+    return m;
+}
+
+void ptq8_model_free(ptq8_model* m) { delete m; }
+
+int ptq8_model_info(const ptq8_model* mm, int* out) {
+    if (!mm || !out) return PTQ8_ERR_INVALID;
+    const Model& m = mm->m;
+    int n_dw = 0, n_grouped = 0, n_relu6 = 0, n_res2 = 0;
+    for (const ConvSpec& c : m.convs) {
+        n_dw += c.depthwise();
+        n_grouped += c.groups != 1;
+        n_relu6 += c.relu == 2;
+    }
+    for (const BlockSpec& b : m.blocks) n_res2 += b.residual == 2;
+    out[0] = (int)m.convs.size();
+    out[1] = (int)m.blocks.size();
+    out[2] = m.stem_pool;
+    out[3] = m.fc_in;
+    out[4] = m.fc_out;
+    out[5] = n_dw;
+    out[6] = n_grouped;
+    out[7] = n_relu6;
+    out[8] = n_res2;
+    out[9] = m.magic == "PTQ2" ? 2 : 1;
+    out[10] = m.blocks.empty() ? 0 : (int)m.blocks[0].convs.size();
+    return PTQ8_OK;
+}
+
+int ptq8_model_conv(const ptq8_model* mm, int i, int* meta10) {
+    if (!mm || !meta10 || i < 0 || i >= (int)mm->m.convs.size()) return PTQ8_ERR_INVALID;
+    const ConvSpec& c = mm->m.convs[i];
+    const int v[10] = {c.cout, c.cin, c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, c.relu, c.groups};
+    std::memcpy(meta10, v, sizeof v);
+    return PTQ8_OK;
+}
+
+int ptq8_model_block(const ptq8_model* mm, int i, int* convs, int cap, int* n_convs, int* ds, int* stride,
+                     int* residual) {
+    if (!mm || i < 0 || i >= (int)mm->m.blocks.size()) return PTQ8_ERR_INVALID;
+    const BlockSpec& b = mm->m.blocks[i];
+    if (n_convs) *n_convs = (int)b.convs.size();
+    for (int k = 0; k < (int)b.convs.size() && k < cap && convs; ++k) convs[k] = b.convs[k];
+    if (ds) *ds = b.ds;
+    if (stride) *stride = b.stride;
+    if (residual) *residual = b.residual;
+    return PTQ8_OK;
+}
+
+int ptq8_model_weights(const ptq8_model* mm, int i, const float** weight, size_t* n_weight, const float** bias) {
+    if (!mm || i < -1 || i >= (int)mm->m.convs.size()) return PTQ8_ERR_INVALID;
+    if (i == -1) {
+        if (weight) *weight = mm->m.fc_w.data();
+        if (n_weight) *n_weight = mm->m.fc_w.size();
+        if (bias) *bias = mm->m.fc_b.data();
+        return PTQ8_OK;
+    }
+    const ConvSpec& c = mm->m.convs[i];
+    if (weight) *weight = c.weight.data();
+    if (n_weight) *n_weight = c.weight.size();
+    if (bias) *bias = c.bias.data();
+    return PTQ8_OK;
+}
+
+int ptq8_load_ptqc(const char* path, size_t n_expected, float* lohi, size_t cap, char* err, size_t errlen) {
+    if (!path) {
+        copy_err("null path", err, errlen);
+        return PTQ8_ERR_INVALID;
+    }
+    std::vector<std::pair<float, float>> r;
+    std::string e;
+    if (!load_ptqc(path, n_expected, &r, &e)) {
+        copy_err(e, err, errlen);
+        return PTQ8_ERR_FORMAT;
+    }
+    if (lohi) {
+        if (cap < 2 * r.size()) {
+            copy_err("output buffer too small", err, errlen);
+            return PTQ8_ERR_INVALID;
+        }
+        for (size_t k = 0; k < r.size(); ++k) {
+            lohi[2 * k] = r[k].first;
+            lohi[2 * k + 1] = r[k].second;
+        }
+    }
+    copy_err("", err, errlen);
+    return PTQ8_OK;
+}
+
+double ptq8_act_scale(float lo, float hi, int bits, int mode) { return act_scale_from_range(lo, hi, bits, mode); }
+
+int ptq8_quantize_weight(const float* w, int cout, int k, int bits, int8_t* codes, float* scale32) {
+    if (!w || !codes || !scale32 || cout <= 0 || k <= 0 || bits < 2 || bits > 8) return PTQ8_ERR_INVALID;
+    quantize_weight_per_channel(w, cout, k, bits, codes, scale32);
+    return PTQ8_OK;
+}
+
+ptq8_engine* ptq8_engine_create(int device) {
+    auto* e = new ptq8_engine();
+    e->device = device;
+    return e;
+}
+
+void ptq8_engine_destroy(ptq8_engine* e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    delete e;
+}
+
+const char* ptq8_engine_last_error(const ptq8_engine* e) { return e ? e->err.c_str() : "null engine"; }
+
+int ptq8_engine_build(ptq8_engine* e, const ptq8_model* mm, int w_bits, int a_bits, const int* layer_bits,
+                      int n_layer_bits, int passes) {
+    if (!e || !mm) return PTQ8_ERR_INVALID;
+    const Model& m = mm->m;
+    if (a_bits != 8) return e->fail(strf("a_bits=%d unsupported (int8 activations only)", a_bits));
+    if (w_bits != 8 && w_bits != 4) return e->fail(strf("w_bits=%d unsupported (8 or 4)", w_bits));
+    if (layer_bits && n_layer_bits != (int)m.convs.size())
+        return e->fail(strf("layer plan has %d entries but the model has %zu convs", n_layer_bits, m.convs.size()));
+    e->model = &m;
+    e->w_bits = w_bits;
+    e->a_bits = a_bits;
+    e->passes = passes;
+    e->layer_bits.assign(m.convs.size(), w_bits);
+    if (layer_bits)
+        for (size_t i = 0; i < m.convs.size(); ++i) {
+            if (layer_bits[i] != 8 && layer_bits[i] != 4)
+                return e->fail(strf("layer plan: conv %zu bits=%d (4/8 only)", i, layer_bits[i]));
+            e->layer_bits[i] = layer_bits[i];
+        }
+    std::string verr;
+    if (!m.validate(&verr, e->in_h, e->in_w)) return e->fail(verr);
+    e->q.assign(m.convs.size(), ConvQ());
+    for (size_t i = 0; i < m.convs.size(); ++i) {
+        const ConvSpec& c = m.convs[i];
+        ConvQ& cq = e->q[i];
+        cq.spec = c;
+        cq.spec.weight.clear();
+        cq.spec.bias.clear();
+        cq.bits = e->layer_bits[i];
+        const int K = c.cin * c.kh * c.kw;
+        cq.codes.resize((size_t)c.cout * K);
+        cq.wscale.resize(c.cout);
+        quantize_weight_per_channel(c.weight.data(), c.cout, K, cq.bits, cq.codes.data(), cq.wscale.data());
+        cq.bias = c.bias;
+    }
+    // graph passes run on the quantized layers (codes + scales), so they are exact
+    if (passes) {
+        int h = conv_out_dim(e->in_h, m.convs[0].kh, m.convs[0].sh, m.convs[0].ph);
+        int w = conv_out_dim(e->in_w, m.convs[0].kw, m.convs[0].sw, m.convs[0].pw);
+        if (m.stem_pool) { h = (h + 2 - 3) / 2 + 1; w = (w + 2 - 3) / 2 + 1; }
+        for (size_t bi = 0; bi < m.blocks.size(); ++bi) {
+            const BlockSpec& b = m.blocks[bi];
+            auto try_conv = [&](int ci, int ih, int iw) {
+                std::string note;
+                bool done = false;
+                if (passes & PTQ8_PASS_CENTER_TAP) done = center_tap(e->q[ci], ih, iw, &note);
+                if (!done && (passes & PTQ8_PASS_DECOMPOSE)) done = decompose(e->q[ci], ih, iw, &note);
+                e->passes_log.push_back(strf("conv[%d] in %dx%d: %s", ci, ih, iw, done ? note.c_str() : "unchanged"));
+            };
+            if (b.ds >= 0) try_conv(b.ds, h, w);
+            int th = h, tw = w;
+            for (int ci : b.convs) {
+                if (ci < 0) continue;
+                const ConvSpec& c = m.convs[ci];
+                try_conv(ci, th, tw);
+                th = conv_out_dim(th, c.kh, c.sh, c.ph);
+                tw = conv_out_dim(tw, c.kw, c.sw, c.pw);
+            }
+            h = th;
+            w = tw;
+        }
+    }
+    e->built = true;
+    e->planned = false;
+    return PTQ8_OK;
+}
+
+int ptq8_engine_set_act_mode(ptq8_engine* e, int mode) {
+    if (!e) return PTQ8_ERR_INVALID;
+    if (mode != ACT_ABSMAX && mode != ACT_MINMAX) return e->fail("act mode must be 0 (absmax) or 1 (minmax)");
+    e->act_mode = mode;
+    if (e->calibrated) {
+        for (size_t i = 0; i < e->ranges.size(); ++i)
+            e->scale[i] = act_scale_from_range(e->ranges[i].first, e->ranges[i].second, e->a_bits, e->act_mode);
+        e->planned = false;
+    }
+    return PTQ8_OK;
+}
+
+int ptq8_engine_set_calib(ptq8_engine* e, const float* lohi, size_t n) {
+    if (!e) return PTQ8_ERR_INVALID;
+    if (!e->built) return e->fail("set_calib before build");
+    if (n != e->q.size()) return e->fail(strf("calibration layer count %zu != conv count %zu", n, e->q.size()));
+    std::vector<std::pair<float, float>> r(n);
+    for (size_t i = 0; i < n; ++i) {
+        const float lo = lohi[2 * i], hi = lohi[2 * i + 1];
+        if (!std::isfinite(lo) || !std::isfinite(hi)) return e->fail(strf("layer %zu calibration range not finite", i));
+        if (lo > hi) return e->fail(strf("layer %zu calibration range lo > hi", i));
+        r[i] = {lo, hi};
+    }
+    e->ranges = r;
+    e->scale.resize(n);
+    for (size_t i = 0; i < n; ++i) e->scale[i] = act_scale_from_range(r[i].first, r[i].second, e->a_bits, e->act_mode);
+    e->calibrated = true;
+    e->planned = false;
+    return PTQ8_OK;
+}
+
+int ptq8_engine_set_input_shape(ptq8_engine* e, int c, int h, int w) {
+    if (!e || c <= 0 || h <= 0 || w <= 0) return PTQ8_ERR_INVALID;
+    e->in_c = c;
+    e->in_h = h;
+    e->in_w = w;
+    e->planned = false;
+    return PTQ8_OK;
+}
+
+int ptq8_engine_alloc_scratch(ptq8_engine* e, int max_batch) {
+    if (!e) return PTQ8_ERR_INVALID;
+    return finalize(e, max_batch);
+}
+
+int ptq8_engine_set_stream(ptq8_engine* e, void* stream) {
+    if (!e) return PTQ8_ERR_INVALID;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+    if (e->own_stream && e->stream) cudaStreamDestroy(e->stream);
+    e->own_stream = false;
+    e->stream = static_cast<cudaStream_t>(stream);
+    if (!e->stream) {
+        if (!e->cuda_ok(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) return PTQ8_ERR_CUDA;
+        e->own_stream = true;
+    }
+    return PTQ8_OK;
+}
+
+void* ptq8_engine_stream(ptq8_engine* e) { return e ? static_cast<void*>(e->stream) : nullptr; }
+
+float* ptq8_engine_input_buffer(ptq8_engine* e) { return e ? e->d_input : nullptr; }
+float* ptq8_engine_logits_buffer(ptq8_engine* e) { return e ? e->d_logits : nullptr; }
+
+int ptq8_engine_run(ptq8_engine* e, int n, int use_graph) {
+    if (!e) return PTQ8_ERR_INVALID;
+    return launch(e, n, use_graph != 0);
+}
+
+int ptq8_engine_forward_device(ptq8_engine* e, const float* x_dev, int n, float* logits_dev) {
+    if (!e || !x_dev || !logits_dev) return PTQ8_ERR_INVALID;
+    if (!e->planned) {
+        int rc = finalize(e, std::max(n, e->max_batch));
+        if (rc) return rc;
+    }
+    if (n <= 0 || n > e->max_batch) return e->fail(strf("batch %d outside [1, %d]", n, e->max_batch));
+    const size_t in_bytes = (size_t)n * e->in_c * e->in_h * e->in_w * sizeof(float);
+    if (x_dev != e->d_input &&
+        !e->cuda_ok(cudaMemcpyAsync(e->d_input, x_dev, in_bytes, cudaMemcpyDeviceToDevice, e->stream), "input copy"))
+        return PTQ8_ERR_CUDA;
+    int rc = launch(e, n, true);
+    if (rc) return rc;
+    if (logits_dev != e->d_logits &&
+        !e->cuda_ok(cudaMemcpyAsync(logits_dev, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, e->stream),
+                    "logits copy"))
+        return PTQ8_ERR_CUDA;
+    return PTQ8_OK;
+}
+
+int ptq8_engine_forward(ptq8_engine* e, const float* x_host, int n, int c, int h, int w, float* logits_host) {
+    if (!e || !x_host || !logits_host) return PTQ8_ERR_INVALID;
+    if (c != e->in_c || h != e->in_h || w != e->in_w)
+        return e->fail(strf("input shape %dx%dx%d != engine input %dx%dx%d", c, h, w, e->in_c, e->in_h, e->in_w));
+    if (!e->planned) {
+        int rc = finalize(e, std::max(n, e->max_batch));
+        if (rc) return rc;
+    }
+    if (n <= 0 || n > e->max_batch) return e->fail(strf("batch %d outside [1, %d]", n, e->max_batch));
+    const size_t in_bytes = (size_t)n * c * h * w * sizeof(float);
+    if (!e->cuda_ok(cudaMemcpyAsync(e->d_input, x_host, in_bytes, cudaMemcpyHostToDevice, e->stream), "H2D"))
+        return PTQ8_ERR_CUDA;
+    int rc = launch(e, n, true);
+    if (rc) return rc;
+    if (!e->cuda_ok(cudaMemcpyAsync(logits_host, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
+                                    cudaMemcpyDeviceToHost, e->stream),
+                    "D2H"))
+        return PTQ8_ERR_CUDA;
+    if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "forward")) return PTQ8_ERR_CUDA;
+    return ptq8_engine_check_device_error(e);
+}
+
+int ptq8_engine_copy_logits(ptq8_engine* e, int n, float* dst_dev) {
+    if (!e || !dst_dev || !e->planned || n <= 0 || n > e->max_batch) return PTQ8_ERR_INVALID;
+    if (!e->cuda_ok(cudaMemcpyAsync(dst_dev, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, e->stream),
+                    "logits copy"))
+        return PTQ8_ERR_CUDA;
+    return PTQ8_OK;
+}
+
+int ptq8_engine_sync(ptq8_engine* e) {
+    if (!e) return PTQ8_ERR_INVALID;
+    if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "sync")) return PTQ8_ERR_CUDA;
+    return ptq8_engine_check_device_error(e);
+}
+
+int ptq8_engine_check_device_error(ptq8_engine* e) {
+    if (!e) return PTQ8_ERR_INVALID;
+    int v = 0;
+    if (!e->cuda_ok(cudaMemcpyFromSymbol(&v, g_ptq8_error, sizeof(int)), "read device error")) return PTQ8_ERR_CUDA;
+    if (v != 0) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_ptq8_error, &z, sizeof(int));
+        return e->fail(strf("device wait timed out (code %d); results of this forward are invalid", v), PTQ8_ERR_TIMEOUT);
+    }
+    return PTQ8_OK;
+}
+
+int ptq8_engine_tensor_info(ptq8_engine* e, int what, int index, int* shape4) {
+    // what 0: input codes of conv `index` -> (N_max, H, W, ld); what 1: final fp32 map (N_max, H, W, C)
+    if (!e || !e->planned || !shape4) return PTQ8_ERR_INVALID;
+    if (what == 0) {
+        if (index < 0 || index >= (int)e->conv_step.size() || e->conv_step[index] < 0) return PTQ8_ERR_INVALID;
+        const Step& st = e->steps[e->conv_step[index]];
+        if (st.kind == K_STEM_IM2COL) {
+            shape4[0] = e->max_batch; shape4[1] = st.oh; shape4[2] = st.ow; shape4[3] = st.kpad;
+        } else {
+            const Value& v = e->vals[st.in_val];
+            shape4[0] = e->max_batch; shape4[1] = v.h; shape4[2] = v.w; shape4[3] = v.ldq;
+        }
+        return PTQ8_OK;
+    }
+    if (what == 1) {
+        const Value& v = e->vals[e->final_val];
+        shape4[0] = e->max_batch; shape4[1] = v.h; shape4[2] = v.w; shape4[3] = v.c;
+        return PTQ8_OK;
+    }
+    return PTQ8_ERR_INVALID;
+}
+
+int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst, size_t bytes) {
+    if (!e || !e->planned || !host_dst) return PTQ8_ERR_INVALID;
+    int shp[4];
+    int rc = ptq8_engine_tensor_info(e, what, index, shp);
+    if (rc) return rc;
+    const void* src;
+    size_t need;
+    if (what == 0) {
+        const Step& st = e->steps[e->conv_step[index]];
+        if (st.kind == K_STEM_IM2COL) src = st.d_im2col;
+        else {
+            const Value& v = e->vals[st.in_val];
+            src = v.codes[v.code_index(st.s_in)];
+        }
+        need = (size_t)n * shp[1] * shp[2] * shp[3];
+    } else {
+        src = e->vals[e->final_val].f32;
+        need = (size_t)n * shp[1] * shp[2] * shp[3] * sizeof(float);
+    }
+    if (bytes < need) return e->fail("dump buffer too small");
+    if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "sync") ||
+        !e->cuda_ok(cudaMemcpy(host_dst, src, need, cudaMemcpyDeviceToHost), "dump"))
+        return PTQ8_ERR_CUDA;
+    return PTQ8_OK;
+}
+
+int ptq8_engine_profile(ptq8_engine* e, int n, int iters, float* ms, double* macs, double* bytes, int* kind,
+                        int cap, int* n_steps) {
+    if (!e || iters <= 0) return PTQ8_ERR_INVALID;
+    if (!e->planned) {
+        int rc = finalize(e, std::max(n, e->max_batch));
+        if (rc) return rc;
+    }
+    if (n <= 0 || n > e->max_batch) return e->fail("profile: batch outside the allocated range");
+    const int ns = (int)e->steps.size() + 1;
+    if (n_steps) *n_steps = ns;
+    if (cap < ns) return e->fail(strf("profile: needs %d entries", ns));
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    for (int si = 0; si < ns; ++si) {
+        enqueue_step(e, n, si);   // warm
+        cudaEventRecord(a, e->stream);
+        for (int it = 0; it < iters; ++it) enqueue_step(e, n, si);
+        cudaEventRecord(b, e->stream);
+        if (!e->cuda_ok(cudaEventSynchronize(b), "profile")) {
+            cudaEventDestroy(a);
+            cudaEventDestroy(b);
+            return PTQ8_ERR_CUDA;
+        }
+        float t = 0;
+        cudaEventElapsedTime(&t, a, b);
+        if (ms) ms[si] = t / iters;
+        double mc, by;
+        int k;
+        step_work(e, n, si, &mc, &by, &k);
+        if (macs) macs[si] = mc;
+        if (bytes) bytes[si] = by;
+        if (kind) kind[si] = k;
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return ptq8_engine_check_device_error(e);
+}
+
+int ptq8_engine_n_launches(const ptq8_engine* e) {
+    if (!e || !e->planned) return -1;
+    int k = 1;   // head
+    for (const Step& st : e->steps) k += st.kind == K_STEM_IM2COL ? 2 : 1;
+    return k;
+}
+
+int ptq8_engine_passes_log(const ptq8_engine* e, char* out, size_t cap) {
+    if (!e || !out || !cap) return PTQ8_ERR_INVALID;
+    std::string s;
+    for (const std::string& l : e->passes_log) s += l + "\n";
+    std::snprintf(out, cap, "%s", s.c_str());
+    return PTQ8_OK;
+}
+
+}  // extern "C"

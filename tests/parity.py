@@ -1,0 +1,47 @@
+"""Engine-vs-oracle comparison helpers shared by the GPU parity tests."""
+import numpy as np
+
+from oracle import ptq8_oracle as O
+
+
+def stem_rows(codes_nchw: np.ndarray, conv: O.Conv, kpad: int) -> np.ndarray:
+    """Expected stem im2col rows [N, OH, OW, kpad], k = (i*KW + j)*C + c, from oracle codes."""
+    N, C, H, W = codes_nchw.shape
+    OH = (H + 2 * conv.ph - conv.kh) // conv.sh + 1
+    OW = (W + 2 * conv.pw - conv.kw) // conv.sw + 1
+    xp = np.zeros((N, C, H + 2 * conv.ph, W + 2 * conv.pw), dtype=np.int8)
+    xp[:, :, conv.ph:conv.ph + H, conv.pw:conv.pw + W] = codes_nchw
+    out = np.zeros((N, OH, OW, kpad), dtype=np.int8)
+    for i in range(conv.kh):
+        for j in range(conv.kw):
+            tap = xp[:, :, i:i + conv.sh * (OH - 1) + 1:conv.sh, j:j + conv.sw * (OW - 1) + 1:conv.sw]
+            k0 = (i * conv.kw + j) * C
+            out[..., k0:k0 + C] = tap.transpose(0, 2, 3, 1)
+    return out
+
+
+def compare(engine, trace: O.Trace, model: O.Model, n: int, logits: np.ndarray, rtol: float = 1e-5):
+    """Assert bit-exact int8 conv-input codes and final fp32 map; logits within rtol."""
+    bad = []
+    for i, conv in enumerate(model.convs):
+        got = engine.dump_codes(i, n)
+        want = trace.codes[i]
+        if i == model.stem:
+            exp = stem_rows(want, conv, got.shape[-1])
+            ok = np.array_equal(got, exp)
+        else:
+            C = want.shape[1]
+            ok = np.array_equal(got[..., :C], want.transpose(0, 2, 3, 1))
+            if not ok:
+                d = got[..., :C].astype(np.int32) - want.transpose(0, 2, 3, 1)
+                bad.append((i, int((d != 0).sum()), int(np.abs(d).max()), d.size))
+                continue
+        if not ok:
+            bad.append((i, -1, -1, got.size))
+    assert not bad, f"int8 code mismatches (conv, n_diff, max|diff|, size): {bad}"
+    fin = engine.dump_final(n)
+    want = trace.block_out[-1].transpose(0, 2, 3, 1) if trace.block_out else trace.stem_out.transpose(0, 2, 3, 1)
+    assert np.array_equal(fin, want), f"final fp32 map differs: max|diff|={np.abs(fin - want).max()}"
+    ok, err = O.logits_close(logits, trace.logits, rtol)
+    assert ok, f"logits rel err {err:.3e} > {rtol}"
+    return err

@@ -1,0 +1,48 @@
+"""Bit-exact parity of the sm_100a engine with the CPU oracle (through the C ABI)."""
+import numpy as np
+import pytest
+
+from oracle import ptq8_oracle as O
+from tests.parity import compare
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(paths, n, seed=7, passes=0, scale=1.0):
+    from ptq_int8_lab_b200 import engine as E
+    m = E.Model.load(paths["model"])
+    ranges = E.load_ptqc(paths["calib"], m.n_conv)
+    bits = E.load_layer_plan(paths["plan"], m.n_conv)
+    eng = E.Int8Engine(0)
+    eng.build(m, 8, 8, layer_bits=bits, passes=passes)
+    eng.set_calib(ranges)
+    eng.alloc_scratch(max(n, 8))
+    x = (np.random.default_rng(seed).standard_normal((n, 3, 32, 32)) * scale).astype(np.float32)
+    logits = eng.forward(x)
+    om = O.read_model(paths["model"])
+    orc = O.Oracle(om, O.read_ptqc(paths["calib"]), layer_bits=bits)
+    tr = orc.forward(x)
+    return eng, tr, om, logits
+
+
+@pytest.mark.parametrize("cfg", [0, 2, 3])
+def test_config_models(make_model, cfg):
+    paths = make_model(cfg)
+    eng, tr, om, logits = _run(paths, 6)
+    compare(eng, tr, om, 6, logits)
+
+
+@pytest.mark.parametrize("key,kw", [("resnet18", dict(seed=0, bn="data")),
+                                    ("mobilenet_v2", dict(seed=1, bn="data")),
+                                    ("mobilenet_v2", dict(seed=2, bn="data", mixed=True))])
+def test_normalized_models(make_model, key, kw):
+    paths = make_model(key, **kw)
+    eng, tr, om, logits = _run(paths, 5, seed=11)
+    compare(eng, tr, om, 5, logits)
+
+
+def test_ragged_batch(make_model):
+    """Batch not a multiple of the M-tile image count (layer3 packs 2 images, layer4 8)."""
+    paths = make_model("resnet18", seed=0, bn="data")
+    eng, tr, om, logits = _run(paths, 13, seed=3)
+    compare(eng, tr, om, 13, logits)
