@@ -204,7 +204,9 @@ def main():
     paths = model_files(a.model_cache, rank, world, barrier)
     B = a.batch
     eng = E.open_engine(paths["model"], paths["calib"], paths["plan"], max_batch=B, device=local)
-    stream = torch.cuda.current_stream()
+    # a real (non-legacy) stream shared by the engine, torch events and NCCL
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     eng.set_stream(stream.cuda_stream)
 
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
@@ -246,6 +248,13 @@ def main():
 
     # ---- per-launch profile (device events per step) -> roofline of the dense convs
     prof = eng.profile(B, iters=3)
+    if os.environ.get("PTQ8_BENCH_LAYERS"):
+        kinds = {0: "stem", 1: "conv_tc", 2: "dw", 3: "maxpool", 4: "head"}
+        for p in prof:
+            t = p["ms"] / 1e3
+            print(f"[layer] step {p['step']:2d} {kinds[p['kind']]:8s} {p['ms']:8.3f} ms  "
+                  f"{2 * p['macs'] / t / 1e12 if t else 0:8.1f} TOPS  {p['bytes'] / t / 1e9 if t else 0:8.1f} GB/s",
+                  file=sys.stderr)
     tc = [p for p in prof if p["kind"] in (0, 1)]
     tc_ms = sum(p["ms"] for p in tc)
     tc_ops = sum(2.0 * p["macs"] for p in tc)

@@ -186,6 +186,19 @@ def conv2d_int8(x: np.ndarray, weight: np.ndarray, bias: Optional[np.ndarray],
     return y, acc, codes
 
 
+def gemm_int8(a: np.ndarray, weight: np.ndarray, bias: Optional[np.ndarray], act_scale: float,
+              w_bits: int = 8, activation: int = 0):
+    """A[M,K] x W[N,K]^T for the symmetric path (ref_int8.py:253-289); returns (y, acc)."""
+    codes = quantize_act(a, act_scale).astype(np.int32)
+    wcode, wscale = quantize_weight_per_channel_sym(weight, w_bits)
+    acc = int_matmul(codes, wcode.reshape(weight.shape[0], -1).T)
+    factor = np.float32(act_scale) * wscale.astype(np.float32)
+    y = acc.astype(np.float32) * factor[None, :]
+    if bias is not None:
+        y = y + np.asarray(bias, dtype=np.float32)[None, :]
+    return apply_activation(y, activation), acc
+
+
 def maxpool3x3s2p1(x: np.ndarray) -> np.ndarray:
     """Stem maxpool with -inf padding (ref_e2e.py:192-203)."""
     N, C, H, W = x.shape

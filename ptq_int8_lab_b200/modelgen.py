@@ -509,8 +509,8 @@ def qdq_weights(model: nn.Module, bits_by_name: Dict[str, int], fc_bits: Optiona
         flat = w.reshape(w.shape[0], -1)
         scale = np.maximum(np.abs(flat).max(axis=1) / qmax, 1e-8)
         v = flat / scale[:, None]
-        code = np.clip(np.where(v >= 0, np.floor(v + 0.5), np.ceil(v - 0.5)), -(qmax + 1), qmax)
-        deq = code.astype(np.float32) * scale.astype(np.float32)[:, None]
+        code = np.clip(np.where(v >= 0, np.floor(v + 0.5), np.ceil(v - 0.5)), -(qmax + 1), qmax).astype(np.int8)
+        deq = code.astype(np.float32) * scale.astype(np.float32)[:, None]   # int8 codes: no -0.0 weights
         m.weight.data.copy_(torch.from_numpy(deq.reshape(w.shape)))
 
 
