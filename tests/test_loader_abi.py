@@ -34,6 +34,12 @@ def _conv(cout, cin, kh, kw, sh=1, sw=1, ph=0, pw=0, relu=0, groups=1, base=0.0)
     return struct.pack("<10i", cout, cin, kh, kw, sh, sw, ph, pw, relu, groups) + w.tobytes() + b.tobytes()
 
 
+def _load(tmp_path, blob, name="m.bin"):
+    p = tmp_path / name
+    p.write_bytes(blob)
+    return E.Model.load(p)
+
+
 def _valid_mv2_like(ncp=3):
     convs = [_conv(8, 3, 3, 3, 1, 1, 1, 1, relu=2), _conv(8, 1, 3, 3, 1, 1, 1, 1, relu=2, groups=8),
              _conv(8, 8, 1, 1), _conv(16, 8, 1, 1, relu=2), _conv(16, 1, 3, 3, 2, 2, 1, 1, relu=2, groups=16),
