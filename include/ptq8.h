@@ -72,6 +72,11 @@ double ptq8_act_scale(float lo, float hi, int bits, int mode);
 /* quantize_weight_per_channel_sym (ptq_quant.h:72-110): w[cout][k] -> codes, f32 scales. */
 int ptq8_quantize_weight(const float* w, int cout, int k, int bits, int8_t* codes, float* scale32);
 
+/* Activation codes computed on `device` by the engine's own device quantizer
+ * (the epilogue path): codes[i] = clip(round_half_away(double(x[i]) / s), -128, 127)
+ * with s = ptq8_act_scale(lo, hi, 8, mode) (ref_int8.py:89-91).  Test entry point. */
+int ptq8_quantize_device(int device, const float* x_host, size_t n, float lo, float hi, int mode, int8_t* codes);
+
 /* ---- engine ---------------------------------------------------------------- */
 
 /* Int8Engine construction on CUDA device `device` (int8_engine.cuh:130). */

@@ -30,7 +30,6 @@ using namespace ptq8;
 
 namespace {
 
-constexpr int kStages = 4;
 
 std::string strf(const char* f, ...) {
     char buf[1024];
@@ -88,6 +87,9 @@ struct Step {
     int ih = 0, iw = 0, ic = 0, oh = 0, ow = 0, oc = 0;
     int kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0;
     int cb = 32, bn = 16, n_ntiles = 1, ktot = 0, kpad = 0;
+    int stages = 4, b_resident = 0, n_kchunks = 1;
+    size_t smem = 0;
+    int grid_x = 1;
     int TW = 1, TH = 1, TN = 1;
     double s_in = 1.0;
     // device parameters
@@ -301,10 +303,20 @@ void tile_shape(int N, int OH, int OW, int* TW, int* TH, int* TN) {
 
 int choose_cb(int cpad) { return cpad % 128 == 0 ? 128 : (cpad % 64 == 0 ? 64 : 32); }
 
+// N tile: the whole Cout when it fits one MMA (N <= 256, multiple of 16);
+// otherwise equal tiles rounded up to 32 channels, so that every tile's first
+// channel keeps the 32-byte alignment of the epilogue's vector stores.
 void choose_bn(int cout, int* bn, int* ntiles) {
-    const int nt = (cout + 255) / 256;
+    if (cout <= 256) {
+        *ntiles = 1;
+        *bn = round_up(cout, 16);
+        return;
+    }
+    int nt = (cout + 255) / 256;
+    int b = round_up((cout + nt - 1) / nt, 32);
+    nt = (cout + b - 1) / b;
     *ntiles = nt;
-    *bn = round_up((cout + nt - 1) / nt, 16);
+    *bn = b;
 }
 
 int plan(ptq8_engine* e) {
@@ -429,8 +441,45 @@ bool make_map(ptq8_engine* e, CUtensorMap* map, CUtensorMapDataType dt, int rank
     return true;
 }
 
-size_t conv_smem_bytes(int cb, int bn) {
-    return (size_t)kStages * (128 * cb + round_up(bn * cb, 1024)) + 1024 + 8 * (2 * kStages + 1) + 16 + 2 * 4 * round_up(bn, 32) + 64;
+constexpr size_t kSmemBudget = 225 * 1024;
+
+// Dynamic shared memory of conv_tc_kernel for a pipeline shape.
+size_t conv_smem_bytes(int cb, int bn, int stages, int b_chunks) {
+    const size_t sb = (size_t)round_up(bn * cb, 1024);
+    return 1024 + (size_t)stages * 128 * cb + (size_t)b_chunks * sb + 8 * (size_t)round_up(bn, 32);
+}
+
+// Keep the whole weight slab of the N tile resident when it fits next to a
+// pipeline of at least 4 A stages; otherwise stream weights with A.
+void choose_pipeline(Step& st) {
+    for (int S : {24, 20, 16, 12, 10, 8, 6, 5, 4}) {
+        if (S * 128 * st.cb > 96 * 1024) continue;   // 96 KB of A in flight is plenty
+        const size_t b = conv_smem_bytes(st.cb, st.bn, S, st.n_kchunks);
+        if (b <= kSmemBudget) {
+            st.stages = S;
+            st.b_resident = 1;
+            st.smem = b;
+            return;
+        }
+    }
+    for (int S : {16, 12, 10, 8, 6, 5, 4, 3, 2}) {
+        const size_t b = conv_smem_bytes(st.cb, st.bn, S, S);
+        if (b <= kSmemBudget) {
+            st.stages = S;
+            st.b_resident = 0;
+            st.smem = b;
+            return;
+        }
+    }
+    st.stages = 2;
+    st.b_resident = 0;
+    st.smem = conv_smem_bytes(st.cb, st.bn, 2, 2);
+}
+
+int acc_cols_for(int bn) {
+    int tc = 32;
+    while (tc < bn) tc <<= 1;
+    return tc;
 }
 
 int finalize(ptq8_engine* e, int max_batch) {
@@ -515,6 +564,8 @@ int finalize(ptq8_engine* e, int max_batch) {
         }
         st.cb = choose_cb(cpad);
         choose_bn(c.cout, &st.bn, &st.n_ntiles);
+        if (st.n_ntiles > 1 && st.bn % 32 != 0)
+            return e->fail(strf("conv[%d]: N tile %d breaks the 32-byte store alignment", st.conv, st.bn));
         if (!e->dalloc(&st.d_w, w.size(), "alloc weights")) return PTQ8_ERR_CUDA;
         cudaMemcpy(st.d_w, w.data(), w.size(), cudaMemcpyHostToDevice);
         {
@@ -527,6 +578,10 @@ int finalize(ptq8_engine* e, int max_batch) {
                 return PTQ8_ERR_CUDA;
         }
         tile_shape(max_batch, st.oh, st.ow, &st.TW, &st.TH, &st.TN);
+        st.n_kchunks = st.kind == K_STEM_IM2COL ? st.kpad / st.cb : st.kh * st.kw * (cpad / st.cb);
+        choose_pipeline(st);
+        if (st.smem > kSmemBudget)
+            return e->fail(strf("conv[%d]: no pipeline fits in shared memory", st.conv));
         if (st.kind == K_STEM_IM2COL) {
             // the im2col rows form a [N][OH][OW][kpad] map read as a 1x1 conv
             cuuint64_t dims[4] = {(cuuint64_t)st.kpad, (cuuint64_t)st.ow, (cuuint64_t)st.oh, (cuuint64_t)max_batch};
@@ -553,11 +608,23 @@ int finalize(ptq8_engine* e, int max_batch) {
         }
     }
     {
-        const int mx = (int)conv_smem_bytes(128, 256);
-        if (!e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<32, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr") ||
-            !e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<64, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr") ||
-            !e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<128, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr"))
+        const int mx = (int)kSmemBudget;
+        if (!e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr") ||
+            !e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr") ||
+            !e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr"))
             return PTQ8_ERR_CUDA;
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, e->device);
+        for (Step& st : e->steps) {
+            if (st.kind != K_TC && st.kind != K_STEM_IM2COL) continue;
+            int occ = 1;
+            if (st.cb == 128) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, conv_tc_kernel<128>, kConvThreads, st.smem);
+            else if (st.cb == 64) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, conv_tc_kernel<64>, kConvThreads, st.smem);
+            else cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, conv_tc_kernel<32>, kConvThreads, st.smem);
+            const int occ_tmem = 512 / (2 * acc_cols_for(st.bn));
+            occ = std::max(1, std::min(occ, occ_tmem));
+            st.grid_x = std::max(1, sms * occ / st.n_ntiles);
+        }
     }
     if (!e->stream) {
         if (!e->cuda_ok(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) return PTQ8_ERR_CUDA;
@@ -576,6 +643,7 @@ EpiParams epi_for(ptq8_engine* e, const Step& st) {
     p.residual = st.res_val >= 0 ? e->vals[st.res_val].f32 : nullptr;
     p.out_f32 = out.need_f32 ? out.f32 : nullptr;
     p.cout = st.kind == K_MAXPOOL ? out.c : st.oc;
+    p.vec32 = (p.cout % 8 == 0) ? 1 : 0;   // 32-byte aligned fp32 rows
     p.act = st.act;
     p.post = st.res_val >= 0 ? st.post : 0;
     p.out_q0 = out.codes.size() > 0 ? out.codes[0] : nullptr;
@@ -615,11 +683,12 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     }
     if (st.kind == K_STEM_IM2COL) {
         const ConvSpec& c = e->q[st.conv].spec;
-        const size_t words = (size_t)n * st.oh * st.ow * (st.kpad / 4);
-        const int grid = (int)std::min<size_t>((words + 255) / 256, 148 * 64);
-        stem_im2col_kernel<<<grid, 256, 0, s>>>(e->d_input, st.d_im2col, n, c.cin, st.ih, st.iw, st.oh, st.ow,
-                                                c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad,
-                                                (float)(1.0 / st.s_in), st.s_in);
+        const int rows = std::max(1, std::min(st.oh, 4096 / std::max(1, st.ow * st.kpad / 4)));
+        const int bands = (st.oh + rows - 1) / rows;
+        const size_t band_bytes = (size_t)c.cin * ((rows - 1) * c.sh + c.kh) * ((st.ow - 1) * c.sw + c.kw);
+        stem_im2col_kernel<<<n * bands, 256, band_bytes, s>>>(e->d_input, st.d_im2col, n, c.cin, st.ih, st.iw, st.oh,
+                                                              st.ow, c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad,
+                                                              rows, (float)(1.0 / st.s_in), st.s_in);
     }
     ConvGeom g{};
     g.N = n;
@@ -629,29 +698,28 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.tiles_w = (st.ow + st.TW - 1) / st.TW;
     g.tiles_h = (st.oh + st.TH - 1) / st.TH;
     const int tiles_n = (n + st.TN - 1) / st.TN;
+    g.m_tiles = g.tiles_w * g.tiles_h * tiles_n;
     if (st.kind == K_STEM_IM2COL) {
         g.KW = 1; g.SH = 1; g.SW = 1; g.PH = 0; g.PW = 0;
         g.n_cchunks = st.kpad / st.cb;
-        g.n_kchunks = g.n_cchunks;
     } else {
         g.KW = st.kw; g.SH = st.sh; g.SW = st.sw; g.PH = st.ph; g.PW = st.pw;
         g.n_cchunks = e->vals[st.in_val].ldq / st.cb;
-        g.n_kchunks = st.kh * st.kw * g.n_cchunks;
     }
+    g.n_kchunks = st.n_kchunks;
     g.BN = st.bn;
-    int tc = 32;
-    while (tc < st.bn) tc <<= 1;
-    g.tmem_cols = tc;
+    g.acc_cols = acc_cols_for(st.bn);
+    g.stages = st.stages;
+    g.b_resident = st.b_resident;
     g.a_bytes = (uint32_t)(st.TW * st.TH * st.TN * st.cb);
     g.b_bytes = (uint32_t)(st.bn * st.cb);
-    dim3 grid((unsigned)(g.tiles_w * g.tiles_h * tiles_n), (unsigned)st.n_ntiles);
-    const size_t smem = conv_smem_bytes(st.cb, st.bn);
+    dim3 grid((unsigned)std::min(g.m_tiles, st.grid_x), (unsigned)st.n_ntiles);
     if (st.cb == 128)
-        conv_tc_kernel<128, kStages><<<grid, kConvThreads, smem, s>>>(st.map_a, st.map_b, g, ep);
+        conv_tc_kernel<128><<<grid, kConvThreads, st.smem, s>>>(st.map_a, st.map_b, g, ep);
     else if (st.cb == 64)
-        conv_tc_kernel<64, kStages><<<grid, kConvThreads, smem, s>>>(st.map_a, st.map_b, g, ep);
+        conv_tc_kernel<64><<<grid, kConvThreads, st.smem, s>>>(st.map_a, st.map_b, g, ep);
     else
-        conv_tc_kernel<32, kStages><<<grid, kConvThreads, smem, s>>>(st.map_a, st.map_b, g, ep);
+        conv_tc_kernel<32><<<grid, kConvThreads, st.smem, s>>>(st.map_a, st.map_b, g, ep);
 }
 
 int enqueue(ptq8_engine* e, int n) {
@@ -838,6 +906,31 @@ int ptq8_quantize_weight(const float* w, int cout, int k, int bits, int8_t* code
     if (!w || !codes || !scale32 || cout <= 0 || k <= 0 || bits < 2 || bits > 8) return PTQ8_ERR_INVALID;
     quantize_weight_per_channel(w, cout, k, bits, codes, scale32);
     return PTQ8_OK;
+}
+
+int ptq8_quantize_device(int device, const float* x_host, size_t n, float lo, float hi, int mode, int8_t* codes) {
+    if (!x_host || !codes) return PTQ8_ERR_INVALID;
+    if (cudaSetDevice(device) != cudaSuccess) return PTQ8_ERR_CUDA;
+    const double s = act_scale_from_range(lo, hi, 8, mode);
+    float* dx = nullptr;
+    int8_t* dq = nullptr;
+    const size_t nn = n ? n : 1;
+    if (cudaMalloc(&dx, nn * 4) != cudaSuccess) return PTQ8_ERR_CUDA;
+    if (cudaMalloc(&dq, nn + 32) != cudaSuccess) {
+        cudaFree(dx);
+        return PTQ8_ERR_CUDA;
+    }
+    int rc = PTQ8_OK;
+    if (cudaMemcpy(dx, x_host, n * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = PTQ8_ERR_CUDA;
+    if (!rc && n) {
+        const size_t groups = (n + 31) / 32;
+        quantize_kernel<<<(unsigned)((groups + 127) / 128), 128>>>(dx, n, (float)(1.0 / s), s, dq);
+        if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) rc = PTQ8_ERR_CUDA;
+    }
+    if (!rc && cudaMemcpy(codes, dq, n, cudaMemcpyDeviceToHost) != cudaSuccess) rc = PTQ8_ERR_CUDA;
+    cudaFree(dx);
+    cudaFree(dq);
+    return rc;
 }
 
 ptq8_engine* ptq8_engine_create(int device) {

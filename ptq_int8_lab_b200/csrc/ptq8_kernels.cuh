@@ -58,6 +58,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -168,26 +172,101 @@ __host__ __device__ constexpr uint32_t make_idesc_i8(int n) {
 
 // ------------------------------------------------------------------ exact quantize
 
-// Exact int8 code of x for scale s (s64) with inv = float(1/s):
-// clip(round_half_away(double(x)/s), -128, 127).  The float estimate t = x*inv
-// is within 2e-5 of x/s for |x/s| <= 129; whenever t is more than 1e-4 away
-// from a half-integer its nearest integer is the reference's code, otherwise
-// the reference's double-precision formula is evaluated.
-__device__ __forceinline__ int quant_code(float x, float inv, double s) {
-    const float t = __fmul_rn(x, inv);
-    const float r = rintf(t);
-    if (fabsf(__fsub_rn(t, r)) < 0.4999f) {
-        return static_cast<int>(fminf(fmaxf(r, -128.0f), 127.0f));
-    }
-    const double v = static_cast<double>(x) / s;
+// Four ints -> four saturated int8 in byte order a, b, c, d.
+// cvt.pack.sat.s8.s32.b32 d, x, y, z gives {z[15:0], sat(x), sat(y)}.
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    uint32_t out;
+    asm("{\n\t.reg .b32 t;\n\t"
+        "cvt.pack.sat.s8.s32.b32 t, %4, %3, 0;\n\t"
+        "cvt.pack.sat.s8.s32.b32 %0, %2, %1, t;\n\t}\n"
+        : "=r"(out)
+        : "r"(a), "r"(b), "r"(c), "r"(d));
+    return out;
+}
+
+__device__ __forceinline__ int8_t sat8(int q) { return static_cast<int8_t>(min(max(q, -128), 127)); }
+
+// Exact int8 code (as an int) of one value: the fast estimate unless it is near a tie.
+__device__ __forceinline__ int quant_code(float x, float inv, double s);
+
+// 1.5 * 2^23: for |v| < 2^22, v + kRoundMagic lands in [2^23, 2^24) where the
+// float spacing is 1, so the addition rounds v to the nearest integer (ties to
+// even) and the integer is the low mantissa bits.
+constexpr float kRoundMagic = 12582912.0f;
+constexpr int kRoundMagicBits = 0x4B400000;
+
+// int32 accumulator -> float, exact for |acc| < 2^22 (then equal to the RNE
+// conversion); *flag is raised when acc is outside that range.
+__device__ __forceinline__ float acc_to_float(uint32_t acc, uint32_t& flag) {
+    flag |= (acc + 0x400000u) >= 0x800000u;
+    return __fsub_rn(__int_as_float(static_cast<int>(acc) + kRoundMagicBits), kRoundMagic);
+}
+
+// Code estimate of y for scale 1/inv: nearest integer of t = y*inv clamped to
+// +-4096 (codes saturate far earlier).  *flag is raised when t lies within
+// 1e-4 of a half-integer: there the reference's float64 formula decides.
+__device__ __forceinline__ int quant_fast(float y, float inv, uint32_t& flag) {
+    const float t = fminf(fmaxf(__fmul_rn(y, inv), -4096.0f), 4096.0f);
+    const float m = __fadd_rn(t, kRoundMagic);
+    flag |= fabsf(__fsub_rn(t, __fsub_rn(m, kRoundMagic))) >= 0.4999f;
+    return __float_as_int(m) - kRoundMagicBits;
+}
+
+// Exact reference code of y: clip(round_half_away(double(y) / s), -128, 127).
+__device__ __forceinline__ int quant_exact(float y, double s) {
+    const double v = static_cast<double>(y) / s;
     double q = v >= 0.0 ? floor(v + 0.5) : ceil(v - 0.5);
     q = fmin(fmax(q, -128.0), 127.0);
     return static_cast<int>(q);
 }
 
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-    return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
-           ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
+// Rare path: 32 codes with the exact formula (kept out of line: small hot loop).
+__device__ __noinline__ void quant32_exact(const float* y, double s, uint32_t* w) {
+    for (int j = 0; j < 8; ++j)
+        w[j] = pack4(quant_exact(y[4 * j], s), quant_exact(y[4 * j + 1], s), quant_exact(y[4 * j + 2], s),
+                     quant_exact(y[4 * j + 3], s));
+}
+
+// 32 int8 codes of y (scale s, inv = float(1/s)) packed into 8 words.
+__device__ __forceinline__ void quant32(const float (&y)[32], float inv, double s, uint32_t (&w)[8]) {
+    uint32_t flag = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int a = quant_fast(y[4 * j], inv, flag), b = quant_fast(y[4 * j + 1], inv, flag);
+        const int c = quant_fast(y[4 * j + 2], inv, flag), d = quant_fast(y[4 * j + 3], inv, flag);
+        w[j] = pack4(a, b, c, d);
+    }
+    if (flag) {
+        float ys[32];
+        uint32_t ws[8];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ys[j] = y[j];
+        quant32_exact(ys, s, ws);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = ws[j];
+    }
+}
+
+__device__ __forceinline__ int quant_code(float x, float inv, double s) {
+    uint32_t flag = 0;
+    const int q = quant_fast(x, inv, flag);
+    return flag ? quant_exact(x, s) : q;
+}
+
+__device__ __forceinline__ void ld_v8(const float* p, float* v) {
+    asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+                 : "l"(p));
+}
+__device__ __forceinline__ void st_v8(float* p, const float* v) {
+    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]), "f"(v[1]),
+                 "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void st_v8(uint32_t* p, const uint32_t* v) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]),
+                 "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 
 __device__ __forceinline__ float apply_act(float y, int act) {
@@ -209,28 +288,30 @@ struct EpiParams {
     float inv0, inv1;
     double s0, s1;
     int cout;
+    int vec32; // 1 when fp32 rows are 32-byte aligned (cout % 8 == 0): 256-bit loads/stores allowed
     int act;   // activation of the conv itself: 0 none / 1 relu / 2 relu6
     int post;  // residual: 0 none, 1 add then relu, 2 add only
 };
 
-// Finish 32 consecutive channels [c0, c0+32) of output position p (nv of them valid).
-__device__ __forceinline__ void epilogue_store32(const EpiParams& e, size_t p, int c0, int nv, float (&y)[32]) {
+// Residual of 32 consecutive channels [c0, c0+32) of output position p (nv valid).
+__device__ __forceinline__ void load_res32(const EpiParams& e, size_t p, int c0, int nv, float (&r)[32]) {
+    const float* rp = e.residual + p * e.cout + c0;
+    if (nv == 32 && e.vec32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) ld_v8(rp + j, &r[j]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = j < nv ? rp[j] : 0.0f;
+    }
+}
+
+// Finish 32 consecutive channels [c0, c0+32) of output position p (nv of them valid):
+// residual add (values in r) + post activation, fp32 store, int8 codes per consumer scale.
+__device__ __forceinline__ void epilogue_store32(const EpiParams& e, size_t p, int c0, int nv, float (&y)[32],
+                                                 const float (&r)[32]) {
     if (e.post != 0) {
-        const float* rp = e.residual + p * e.cout + c0;
-        if (nv == 32) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                float4 r = __ldg(reinterpret_cast<const float4*>(rp + j));
-                y[j] = __fadd_rn(y[j], r.x);
-                y[j + 1] = __fadd_rn(y[j + 1], r.y);
-                y[j + 2] = __fadd_rn(y[j + 2], r.z);
-                y[j + 3] = __fadd_rn(y[j + 3], r.w);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (j < nv) y[j] = __fadd_rn(y[j], rp[j]);
-        }
+        for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(y[j], r[j]);
         if (e.post == 1) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) y[j] = fmaxf(y[j], 0.0f);
@@ -238,10 +319,9 @@ __device__ __forceinline__ void epilogue_store32(const EpiParams& e, size_t p, i
     }
     if (e.out_f32) {
         float* op = e.out_f32 + p * e.cout + c0;
-        if (nv == 32) {
+        if (nv == 32 && e.vec32) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(op + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+            for (int j = 0; j < 32; j += 8) st_v8(op + j, &y[j]);
         } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -257,16 +337,12 @@ __device__ __forceinline__ void epilogue_store32(const EpiParams& e, size_t p, i
         int8_t* qp = qbase + p * static_cast<size_t>(o == 0 ? e.ldq0 : e.ldq1) + c0;
         if (nv == 32) {
             uint32_t w[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                w[j] = pack4(quant_code(y[4 * j], inv, s), quant_code(y[4 * j + 1], inv, s),
-                             quant_code(y[4 * j + 2], inv, s), quant_code(y[4 * j + 3], inv, s));
-            reinterpret_cast<uint4*>(qp)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            reinterpret_cast<uint4*>(qp)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            quant32(y, inv, s, w);
+            st_v8(reinterpret_cast<uint32_t*>(qp), w);
         } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-                if (j < nv) qp[j] = static_cast<int8_t>(quant_code(y[j], inv, s));
+                if (j < nv) qp[j] = sat8(quant_code(y[j], inv, s));
         }
     }
 }
@@ -277,66 +353,77 @@ struct ConvGeom {
     int N, OH, OW;              // output map (per image)
     int TW, TH, TN;             // one M tile = TN images x TH rows x TW cols (<= 128 positions)
     int tiles_w, tiles_h;       // M tiles along W and H
+    int m_tiles;                // total M tiles
     int KW, SH, SW, PH, PW;     // kernel width, strides, paddings
     int n_cchunks, n_kchunks;   // channel chunks per tap, total K chunks
     int BN;                     // N tile (multiple of 16, <= 256)
-    int tmem_cols;              // power of two >= max(32, BN)
-    uint32_t a_bytes, b_bytes;  // TMA bytes per stage
+    int acc_cols;               // TMEM columns per accumulator buffer (power of two >= max(32, BN))
+    int stages;                 // A (and streamed B) pipeline depth, <= kMaxStages
+    int b_resident;             // 1: the CTA's whole weight slab stays in shared memory
+    uint32_t a_bytes, b_bytes;  // TMA bytes per A stage / per B chunk
 };
 
-constexpr int kConvThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr int kConvThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiWarps = 8;
+constexpr int kMaxStages = 24;
 
-template <int CB, int STAGES>
+// Persistent implicit-GEMM conv.  grid = (CTAs per N tile, N tiles); each CTA
+// walks M tiles blockIdx.x, blockIdx.x + gridDim.x, ...  Two TMEM accumulators
+// let the epilogue of tile i overlap the MMAs of tile i+1.
+template <int CB>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const ConvGeom g, const EpiParams e) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_abort;
+    __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 6];   // a_full, a_empty, b_full, acc_full[2], acc_empty[2], done
+    __shared__ uint32_t tslot;
     // A wait of an earlier CTA already ran out: skip the work (block-uniform decision).
     if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile int*>(&g_ptq8_error);
     __syncthreads();
     if (s_abort) return;
+
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int BN = g.BN;
     const int bn32 = (BN + 31) & ~31;
-    const int sb_stride = (BN * CB + 1023) & ~1023;   // every stage 1024-byte aligned (swizzle atoms)
+    const int S = g.stages;
+    const int sb_stride = (BN * CB + 1023) & ~1023;   // every B chunk 1024-byte aligned (swizzle atoms)
     uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * 128 * CB;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * sb_stride);  // full[S], empty[S], acc
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
-    float* s_factor = reinterpret_cast<float*>(tslot + 4);
+    uint8_t* sB = smem + S * 128 * CB;
+    float* s_factor = reinterpret_cast<float*>(sB + (g.b_resident ? g.n_kchunks : S) * sb_stride);
     float* s_bias = s_factor + bn32;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int mt = blockIdx.x;
     const int nt = blockIdx.y;
-    const int tw_i = mt % g.tiles_w;
-    const int rest = mt / g.tiles_w;
-    const int th_i = rest % g.tiles_h;
-    const int tn_i = rest / g.tiles_h;
-    const int w0 = tw_i * g.TW, h0 = th_i * g.TH, n0 = tn_i * g.TN;
-
-    const uint32_t full0 = smem_u32(bars);
-    const uint32_t empty0 = smem_u32(bars + STAGES);
-    const uint32_t accbar = smem_u32(bars + 2 * STAGES);
+    const uint32_t full0 = smem_u32(&bars[0]);
+    const uint32_t empty0 = smem_u32(&bars[kMaxStages]);
+    const uint32_t bfull = smem_u32(&bars[2 * kMaxStages]);
+    const uint32_t accf0 = smem_u32(&bars[2 * kMaxStages + 1]);
+    const uint32_t acce0 = smem_u32(&bars[2 * kMaxStages + 3]);
+    const uint32_t donebar = smem_u32(&bars[2 * kMaxStages + 5]);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
-        mbar_init(accbar, 1);
+        mbar_init(bfull, 1);
+        mbar_init(accf0, 1);
+        mbar_init(accf0 + 8, 1);
+        mbar_init(acce0, kEpiWarps);
+        mbar_init(acce0 + 8, kEpiWarps);
+        mbar_init(donebar, 1);
         fence_mbar_init();
         tma_prefetch(&map_a);
         tma_prefetch(&map_b);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tslot), g.tmem_cols);
+        tmem_alloc(smem_u32(&tslot), 2 * g.acc_cols);
         tmem_relinquish();
     }
     if (warp >= 2) {
-        for (int c = threadIdx.x - 64; c < bn32; c += 128) {
+        for (int c = threadIdx.x - 64; c < bn32; c += 32 * kEpiWarps) {
             const int gc = nt * BN + c;
             const bool ok = c < BN && gc < e.cout;
             s_factor[c] = ok ? e.factor[gc] : 0.0f;
@@ -346,123 +433,221 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tslot;
+    const uint32_t tmem = tslot;
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer
-            int issued = 0;
-            for (int kc = 0; kc < g.n_kchunks; ++kc) {
-                const int s = kc % STAGES;
-                const uint32_t ph = (kc / STAGES) & 1;
-                if (!mbar_wait(empty0 + 8 * s, ph ^ 1)) {
-                    atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
-                    break;
-                }
-                const int tap = kc / g.n_cchunks;
-                const int cc = kc - tap * g.n_cchunks;
-                const int ki = tap / g.KW;
-                const int kj = tap - ki * g.KW;
-                mbar_expect_tx(full0 + 8 * s, g.a_bytes + g.b_bytes);
-                tma_load_4d(smem_u32(sA + s * 128 * CB), &map_a, full0 + 8 * s, cc * CB, w0 * g.SW + kj - g.PW,
-                            h0 * g.SH + ki - g.PH, n0);
-                tma_load_2d(smem_u32(sB + s * sb_stride), &map_b, full0 + 8 * s, kc * CB, nt * BN);
-                issued = kc + 1;
+            uint32_t last_ph = 0;   // bit s: parity of the last load issued into stage s
+            uint32_t used = 0;      // bit s: stage s received at least one load
+            bool ok = true;
+            if (g.b_resident) {
+                mbar_expect_tx(bfull, g.b_bytes * g.n_kchunks);
+                for (int kc = 0; kc < g.n_kchunks; ++kc)
+                    tma_load_2d(smem_u32(sB + kc * sb_stride), &map_b, bfull, kc * CB, nt * BN);
             }
-            // Drain: every issued copy must have landed before the CTA can exit.
-            for (int kc = issued > STAGES ? issued - STAGES : 0; kc < issued; ++kc) {
-                if (!mbar_wait(full0 + 8 * (kc % STAGES), (kc / STAGES) & 1)) {
-                    atomicExch(&g_ptq8_error, ERR_DRAIN);
-                    break;
+            int s = 0;
+            uint32_t ph = 0;
+            for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
+                const int tw_i = mt % g.tiles_w;
+                const int rest = mt / g.tiles_w;
+                const int th_i = rest % g.tiles_h;
+                const int tn_i = rest / g.tiles_h;
+                const int w0 = tw_i * g.TW, h0 = th_i * g.TH, n0 = tn_i * g.TN;
+                int tap = 0, cc = 0;
+                for (int kc = 0; kc < g.n_kchunks; ++kc) {
+                    if (!mbar_wait(empty0 + 8 * s, ph ^ 1)) {
+                        atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
+                        ok = false;
+                        break;
+                    }
+                    const int ki = tap / g.KW;
+                    const int kj = tap - ki * g.KW;
+                    const uint32_t fb = full0 + 8 * s;
+                    mbar_expect_tx(fb, g.a_bytes + (g.b_resident ? 0u : g.b_bytes));
+                    tma_load_4d(smem_u32(sA + s * 128 * CB), &map_a, fb, cc * CB, w0 * g.SW + kj - g.PW,
+                                h0 * g.SH + ki - g.PH, n0);
+                    if (!g.b_resident) tma_load_2d(smem_u32(sB + s * sb_stride), &map_b, fb, kc * CB, nt * BN);
+                    last_ph = (last_ph & ~(1u << s)) | (ph << s);
+                    used |= 1u << s;
+                    if (++cc == g.n_cchunks) { cc = 0; ++tap; }
+                    if (++s == S) { s = 0; ph ^= 1; }
                 }
             }
+            // Every issued copy must have landed before the CTA exits.
+            for (int st = 0; st < S; ++st)
+                if ((used >> st) & 1u)
+                    if (!mbar_wait(full0 + 8 * st, (last_ph >> st) & 1u)) {
+                        atomicExch(&g_ptq8_error, ERR_DRAIN);
+                        break;
+                    }
+            if (g.b_resident && !mbar_wait(bfull, 0)) atomicExch(&g_ptq8_error, ERR_DRAIN);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer
             const uint32_t idesc = make_idesc_i8(BN);
-            for (int kc = 0; kc < g.n_kchunks; ++kc) {
-                const int s = kc % STAGES;
-                if (!mbar_wait(full0 + 8 * s, (kc / STAGES) & 1)) {
-                    atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+            bool ok = !g.b_resident || mbar_wait(bfull, 0);
+            if (!ok) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+            int s = 0;
+            uint32_t ph = 0;
+            int t = 0;
+            for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x, ++t) {
+                const int buf = t & 1;
+                const uint32_t use = static_cast<uint32_t>(t >> 1);
+                if (!mbar_wait(acce0 + 8 * buf, (use & 1u) ^ 1u)) {
+                    atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
                     break;
                 }
                 tc_fence_after();
-                const uint64_t da = make_sdesc(smem_u32(sA + s * 128 * CB), CB);
-                const uint64_t db = make_sdesc(smem_u32(sB + s * sb_stride), CB);
+                const uint32_t d = tmem + static_cast<uint32_t>(buf * g.acc_cols);
+                for (int kc = 0; kc < g.n_kchunks; ++kc) {
+                    if (!mbar_wait(full0 + 8 * s, ph)) {
+                        atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t da = make_sdesc(smem_u32(sA + s * 128 * CB), CB);
+                    const uint64_t db =
+                        make_sdesc(smem_u32(sB + (g.b_resident ? kc : s) * sb_stride), CB);
 #pragma unroll
-                for (int k = 0; k < CB / 32; ++k)
-                    mma_i8(tmem, da + 2 * k, db + 2 * k, idesc, (kc | k) != 0 ? 1u : 0u);
-                mma_commit(empty0 + 8 * s);
+                    for (int k = 0; k < CB / 32; ++k)
+                        mma_i8(d, da + 2 * k, db + 2 * k, idesc, (kc | k) != 0 ? 1u : 0u);
+                    mma_commit(empty0 + 8 * s);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                mma_commit(accf0 + 8 * buf);
             }
-            mma_commit(accbar);
+            // all MMAs of this thread complete before TMEM can be released
+            mma_commit(donebar);
+            if (!mbar_wait(donebar, 0)) atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
         }
     } else {
         // ---------------- epilogue: TMEM lanes 32*(warp%4) .. +31 = tile rows
         const int quad = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int tw = g.TW, th = g.TH;
-        const int n = n0 + r / (tw * th);
-        const int h = h0 + (r / tw) % th;
-        const int w = w0 + r % tw;
-        const bool valid = r < tw * th * g.TN && n < g.N && h < g.OH && w < g.OW;
-        const size_t p = (static_cast<size_t>(n) * g.OH + h) * g.OW + w;
-        const bool ok = mbar_wait(accbar, 0);
-        if (!ok) atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
-        tc_fence_after();
+        const int rn = r / (tw * th), rh = (r / tw) % th, rw = r % tw;
+        const bool in_tile = r < tw * th * g.TN;
         const int tile_end = min(e.cout, (nt + 1) * BN);
-        for (int cg = 0; cg < bn32 / 32; ++cg) {
-            uint32_t v[32];
-            tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + cg * 32, v);
-            tmem_wait_ld();
-            const int c0 = nt * BN + cg * 32;
-            if (!ok || !valid || c0 >= tile_end) continue;
-            const int nv = min(32, tile_end - c0);
-            float y[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float a = static_cast<float>(static_cast<int>(v[j]));
-                y[j] = apply_act(__fadd_rn(__fmul_rn(a, s_factor[cg * 32 + j]), s_bias[cg * 32 + j]), e.act);
+        const int ncg = bn32 / 32;
+        int t = 0;
+        for (int mt = blockIdx.x; mt < g.m_tiles; mt += gridDim.x, ++t) {
+            const int buf = t & 1;
+            const uint32_t use = static_cast<uint32_t>(t >> 1);
+            const int tw_i = mt % g.tiles_w;
+            const int rest = mt / g.tiles_w;
+            const int th_i = rest % g.tiles_h;
+            const int tn_i = rest / g.tiles_h;
+            const int n = tn_i * g.TN + rn, h = th_i * g.TH + rh, w = tw_i * g.TW + rw;
+            const bool valid = in_tile && n < g.N && h < g.OH && w < g.OW;
+            const size_t p = (static_cast<size_t>(n) * g.OH + h) * g.OW + w;
+            // the residual does not depend on the MMAs: fetch the first group before waiting
+            float res[32];
+            {
+                const int c0 = nt * BN + half * 32;
+                if (e.post != 0 && valid && half < ncg && c0 < tile_end) load_res32(e, p, c0, min(32, tile_end - c0), res);
             }
-            epilogue_store32(e, p, c0, nv, y);
+            if (!mbar_wait(accf0 + 8 * buf, use & 1u)) {
+                atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
+                break;
+            }
+            tc_fence_after();
+            for (int cg = half; cg < ncg; cg += 2) {
+                uint32_t v[32];
+                __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the per-lane stores
+                tmem_ld32(tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16) +
+                              cg * 32,
+                          v);
+                tmem_wait_ld();
+                const int c0 = nt * BN + cg * 32;
+                if (!valid || c0 >= tile_end) continue;
+                const int nv = min(32, tile_end - c0);
+                float y[32];
+                const float4* f4 = reinterpret_cast<const float4*>(s_factor + cg * 32);
+                const float4* b4 = reinterpret_cast<const float4*>(s_bias + cg * 32);
+                uint32_t big = 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) y[j] = acc_to_float(v[j], big);
+                if (big) {   // |acc| >= 2^22 somewhere: convert with the rounding instruction
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) y[j] = __int2float_rn(static_cast<int>(v[j]));
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 f = f4[j], bb = b4[j];
+                    y[4 * j + 0] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 0], f.x), bb.x), e.act);
+                    y[4 * j + 1] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 1], f.y), bb.y), e.act);
+                    y[4 * j + 2] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 2], f.z), bb.z), e.act);
+                    y[4 * j + 3] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 3], f.w), bb.w), e.act);
+                }
+                epilogue_store32(e, p, c0, nv, y, res);
+                // prefetch the residual of this warp's next column group
+                const int cn = c0 + 64;
+                if (e.post != 0 && cg + 2 < ncg && cn < tile_end) load_res32(e, p, cn, min(32, tile_end - cn), res);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acce0 + 8 * buf);
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, g.tmem_cols);
+    if (warp == 1) tmem_dealloc(tmem, 2 * g.acc_cols);
 }
 
 // ------------------------------------------------------------------ stem im2col
 
 // x: fp32 NCHW [N][C][H][W]; out: int8 [N*OH*OW][kpad] with k = (i*KW + j)*C + c,
 // codes of the stem's scale, zero for out-of-image taps and k >= KH*KW*C.
+// One CTA per band of `rows` output rows of one image: the input band is read
+// once (coalesced), quantized once into shared memory (with zero padding),
+// then the im2col rows are written as consecutive 32-bit words.
 __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restrict__ out, int N, int C, int H,
                                    int W, int OH, int OW, int KH, int KW, int SH, int SW, int PH, int PW,
-                                   int kpad, float inv, double s) {
-    const size_t rows = static_cast<size_t>(N) * OH * OW;
+                                   int kpad, int rows, float inv, double s) {
+    extern __shared__ int8_t band[];   // [C][band_h][band_w]
+    const int bands = (OH + rows - 1) / rows;
+    const int n = blockIdx.x / bands;
+    const int r0 = (blockIdx.x % bands) * rows;
+    const int r1 = min(OH, r0 + rows);
+    const int band_h = (rows - 1) * SH + KH;
+    const int band_w = (OW - 1) * SW + KW;
+    const int ih0 = r0 * SH - PH, iw0 = -PW;
+    for (int idx = threadIdx.x; idx < C * band_h * band_w; idx += blockDim.x) {
+        const int bw = idx % band_w;
+        const int bh = (idx / band_w) % band_h;
+        const int c = idx / (band_w * band_h);
+        const int ih = ih0 + bh, iw = iw0 + bw;
+        int q = 0;
+        if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+            q = sat8(quant_code(__ldg(x + ((static_cast<size_t>(n) * C + c) * H + ih) * W + iw), inv, s));
+        band[idx] = static_cast<int8_t>(q);
+    }
+    __syncthreads();
     const int words = kpad / 4;
-    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < rows * words;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const size_t row = idx / words;
-        const int wd = static_cast<int>(idx - row * words);
-        const int ow = static_cast<int>(row % OW);
-        const int oh = static_cast<int>((row / OW) % OH);
-        const int n = static_cast<int>(row / (static_cast<size_t>(OW) * OH));
-        int q[4];
+    const int K = KH * KW * C;
+    const int total = (r1 - r0) * OW * words;
+    uint32_t* orow = reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(n) * OH + r0) * OW * kpad);
+    for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
+        const int wd = idx % words;
+        const int pos = idx / words;
+        const int ow = pos % OW, ohl = pos / OW;
+        uint32_t packed = 0;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
             const int k = wd * 4 + b;
-            q[b] = 0;
-            if (k < KH * KW * C) {
-                const int c = k % C;
-                const int tap = k / C;
-                const int i = tap / KW, j = tap % KW;
-                const int ih = oh * SH + i - PH, iw = ow * SW + j - PW;
-                if (ih >= 0 && ih < H && iw >= 0 && iw < W)
-                    q[b] = quant_code(__ldg(x + ((static_cast<size_t>(n) * C + c) * H + ih) * W + iw), inv, s);
+            if (k < K) {
+                const int c = k % C, tap = k / C;
+                const int i = tap / KW, j = tap - (tap / KW) * KW;
+                const uint32_t q = static_cast<uint8_t>(band[(c * band_h + ohl * SH + i) * band_w + ow * SW + j]);
+                packed |= q << (8 * b);
             }
         }
-        reinterpret_cast<uint32_t*>(out)[idx] = pack4(q[0], q[1], q[2], q[3]);
+        orow[idx] = packed;
     }
 }
 
@@ -515,9 +700,9 @@ __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int
         if (e.out_f32)
             for (int b = 0; b < nv; ++b) e.out_f32[p * C + c0 + b] = y[b];
         if (e.out_q0)
-            for (int b = 0; b < nv; ++b) e.out_q0[p * e.ldq0 + c0 + b] = static_cast<int8_t>(quant_code(y[b], e.inv0, e.s0));
+            for (int b = 0; b < nv; ++b) e.out_q0[p * e.ldq0 + c0 + b] = sat8(quant_code(y[b], e.inv0, e.s0));
         if (e.out_q1)
-            for (int b = 0; b < nv; ++b) e.out_q1[p * e.ldq1 + c0 + b] = static_cast<int8_t>(quant_code(y[b], e.inv1, e.s1));
+            for (int b = 0; b < nv; ++b) e.out_q1[p * e.ldq1 + c0 + b] = sat8(quant_code(y[b], e.inv1, e.s1));
     }
 }
 
@@ -547,8 +732,29 @@ __global__ void maxpool_kernel(const float* __restrict__ in, int N, int H, int W
             }
         }
         if (e.out_f32) e.out_f32[p * C + c] = m;
-        if (e.out_q0) e.out_q0[p * e.ldq0 + c] = static_cast<int8_t>(quant_code(m, e.inv0, e.s0));
-        if (e.out_q1) e.out_q1[p * e.ldq1 + c] = static_cast<int8_t>(quant_code(m, e.inv1, e.s1));
+        if (e.out_q0) e.out_q0[p * e.ldq0 + c] = sat8(quant_code(m, e.inv0, e.s0));
+        if (e.out_q1) e.out_q1[p * e.ldq1 + c] = sat8(quant_code(m, e.inv1, e.s1));
+    }
+}
+
+// ------------------------------------------------------------------ quantize (test entry)
+
+// codes[i] of x[i] through the same device paths the epilogues use: quant32 on
+// full groups of 32, quant_code on the tail.
+__global__ void quantize_kernel(const float* __restrict__ x, size_t n, float inv, double s, int8_t* __restrict__ out) {
+    const size_t g = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+    const size_t base = g * 32;
+    if (base >= n) return;
+    if (base + 32 <= n) {
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = x[base + j];
+        uint32_t w[8];
+        quant32(y, inv, s, w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) reinterpret_cast<uint32_t*>(out + base)[j] = w[j];
+    } else {
+        for (size_t i = base; i < n; ++i) out[i] = sat8(quant_code(x[i], inv, s));
     }
 }
 

@@ -36,7 +36,7 @@ ACT_MINMAX = 1
 # every symbol include/ptq8.h declares
 EXPORTS = (
     "ptq8_abi_version", "ptq8_model_load", "ptq8_model_free", "ptq8_model_info", "ptq8_model_conv",
-    "ptq8_model_block", "ptq8_model_weights", "ptq8_load_ptqc", "ptq8_act_scale", "ptq8_quantize_weight",
+    "ptq8_model_block", "ptq8_model_weights", "ptq8_load_ptqc", "ptq8_act_scale", "ptq8_quantize_weight", "ptq8_quantize_device",
     "ptq8_engine_create", "ptq8_engine_destroy", "ptq8_engine_last_error", "ptq8_engine_build",
     "ptq8_engine_set_act_mode", "ptq8_engine_set_calib", "ptq8_engine_set_input_shape",
     "ptq8_engine_alloc_scratch", "ptq8_engine_set_stream", "ptq8_engine_stream", "ptq8_engine_forward",
@@ -73,6 +73,8 @@ def lib() -> ctypes.CDLL:
         "ptq8_load_ptqc": (c_int, [c_char_p, c_size, P(ctypes.c_float), c_size, c_char_p, c_size]),
         "ptq8_act_scale": (ctypes.c_double, [ctypes.c_float, ctypes.c_float, c_int, c_int]),
         "ptq8_quantize_weight": (c_int, [P(ctypes.c_float), c_int, c_int, c_int, P(ctypes.c_int8), P(ctypes.c_float)]),
+        "ptq8_quantize_device": (c_int, [c_int, P(ctypes.c_float), c_size, ctypes.c_float, ctypes.c_float, c_int,
+                                         P(ctypes.c_int8)]),
         "ptq8_engine_create": (c_void_p, [c_int]),
         "ptq8_engine_destroy": (None, [c_void_p]),
         "ptq8_engine_last_error": (c_char_p, [c_void_p]),
@@ -205,6 +207,17 @@ def quantize_weight(w: np.ndarray, bits: int = 8) -> Tuple[np.ndarray, np.ndarra
     if rc:
         raise Ptq8Error("quantize_weight: invalid arguments", rc)
     return codes, scale
+
+
+def quantize_device(x: np.ndarray, lo: float, hi: float, mode: int = ACT_ABSMAX, device: int = 0) -> np.ndarray:
+    """int8 codes of x computed by the engine's device quantizer (epilogue code path)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.empty(x.size, dtype=np.int8)
+    rc = lib().ptq8_quantize_device(device, _fptr(x), x.size, lo, hi, mode,
+                                    out.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)))
+    if rc:
+        raise Ptq8Error("ptq8_quantize_device failed", rc)
+    return out
 
 
 # --------------------------------------------------------------------------- engine

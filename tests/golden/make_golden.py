@@ -88,7 +88,9 @@ def make_kats():
     d["gemm_range"] = np.array([float(a.min()), float(a.max())])
     # quantize sweep: dense grid + exact ties + extremes for several scales
     xs = []
+    # ranges as PTQC stores them: float32 values
     for s_lohi in [(-2.0, 4.0), (0.0, 1.2268753), (-3.739, 3.6477), (0.0, 1e-9)]:
+        s_lohi = (float(np.float32(s_lohi[0])), float(np.float32(s_lohi[1])))
         q = SymActQuant.from_range(*s_lohi)
         ks = np.arange(-130, 130) + 0.5
         ties = (ks * q.scale).astype(np.float32)
