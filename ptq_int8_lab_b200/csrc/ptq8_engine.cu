@@ -24,7 +24,7 @@
 
 #include "ptq8_kernels.cuh"
 #include "ptq8_model.hpp"
-#include "../../include/ptq8.h"
+#include "ptq8.h"
 
 using namespace ptq8;
 
@@ -88,6 +88,9 @@ struct Step {
     int kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0;
     int cb = 32, bn = 16, n_ntiles = 1, ktot = 0, kpad = 0;
     int stages = 4, b_resident = 0, n_kchunks = 1;
+    int mode = 0;          // 0 per-tap tile loads, 1 halo block + shifted views (see conv_tc_kernel)
+    int blk_rows = 0;      // mode 1: bordered rows per block
+    int a_stage = 0;       // bytes per A pipeline stage
     size_t smem = 0;
     int grid_x = 1;
     int TW = 1, TH = 1, TN = 1;
@@ -444,36 +447,40 @@ bool make_map(ptq8_engine* e, CUtensorMap* map, CUtensorMapDataType dt, int rank
 constexpr size_t kSmemBudget = 225 * 1024;
 
 // Dynamic shared memory of conv_tc_kernel for a pipeline shape.
-size_t conv_smem_bytes(int cb, int bn, int stages, int b_chunks) {
+size_t conv_smem_bytes(int a_stage, int cb, int bn, int stages, int b_chunks) {
     const size_t sb = (size_t)round_up(bn * cb, 1024);
-    return 1024 + (size_t)stages * 128 * cb + (size_t)b_chunks * sb + 8 * (size_t)round_up(bn, 32);
+    return 1024 + (size_t)stages * a_stage + (size_t)b_chunks * sb + 8 * (size_t)round_up(bn, 32);
 }
 
 // Keep the whole weight slab of the N tile resident when it fits next to a
-// pipeline of at least 4 A stages; otherwise stream weights with A.
-void choose_pipeline(Step& st) {
-    for (int S : {24, 20, 16, 12, 10, 8, 6, 5, 4}) {
-        if (S * 128 * st.cb > 96 * 1024) continue;   // 96 KB of A in flight is plenty
-        const size_t b = conv_smem_bytes(st.cb, st.bn, S, st.n_kchunks);
+// pipeline of at least `min_res` A stages; otherwise stream weights with A.
+// Returns false when mode 1 (which needs resident weights) does not fit.
+bool choose_pipeline(Step& st, int min_res) {
+    for (int S : {24, 20, 16, 12, 10, 8, 6, 5, 4, 3, 2}) {
+        if (S < min_res) break;
+        if ((size_t)S * st.a_stage > 96 * 1024 && S > min_res) continue;   // ~96 KB of A in flight is plenty
+        const size_t b = conv_smem_bytes(st.a_stage, st.cb, st.bn, S, st.n_kchunks);
         if (b <= kSmemBudget) {
             st.stages = S;
             st.b_resident = 1;
             st.smem = b;
-            return;
+            return true;
         }
     }
+    if (st.mode == 1) return false;
     for (int S : {16, 12, 10, 8, 6, 5, 4, 3, 2}) {
-        const size_t b = conv_smem_bytes(st.cb, st.bn, S, S);
+        const size_t b = conv_smem_bytes(st.a_stage, st.cb, st.bn, S, S);
         if (b <= kSmemBudget) {
             st.stages = S;
             st.b_resident = 0;
             st.smem = b;
-            return;
+            return true;
         }
     }
     st.stages = 2;
     st.b_resident = 0;
-    st.smem = conv_smem_bytes(st.cb, st.bn, 2, 2);
+    st.smem = conv_smem_bytes(st.a_stage, st.cb, st.bn, 2, 2);
+    return true;
 }
 
 int acc_cols_for(int bn) {
@@ -504,8 +511,12 @@ int finalize(ptq8_engine* e, int max_batch) {
         v.codes.assign(v.scales.size(), nullptr);
         if (vi == 0) continue;   // network input lives in d_input
         if (v.need_f32 && !e->dalloc(&v.f32, pix * v.c * sizeof(float), "alloc fp32 activation")) return PTQ8_ERR_CUDA;
-        for (size_t k = 0; k < v.scales.size(); ++k)
-            if (!e->dalloc(&v.codes[k], pix * v.ldq, "alloc int8 codes")) return PTQ8_ERR_CUDA;
+        // int8 codes carry a one-pixel zero border (written once, never touched again)
+        const size_t bpix = NB * (v.h + 2) * (v.w + 2);
+        for (size_t k = 0; k < v.scales.size(); ++k) {
+            if (!e->dalloc(&v.codes[k], bpix * v.ldq, "alloc int8 codes")) return PTQ8_ERR_CUDA;
+            if (!e->cuda_ok(cudaMemset(v.codes[k], 0, bpix * v.ldq), "clear codes")) return PTQ8_ERR_CUDA;
+        }
     }
     if (!e->dalloc(&e->d_input, NB * e->in_c * e->in_h * e->in_w * sizeof(float), "alloc input")) return PTQ8_ERR_CUDA;
     if (!e->dalloc(&e->d_logits, NB * m.fc_out * sizeof(float), "alloc logits")) return PTQ8_ERR_CUDA;
@@ -579,7 +590,23 @@ int finalize(ptq8_engine* e, int max_batch) {
         }
         tile_shape(max_batch, st.oh, st.ow, &st.TW, &st.TH, &st.TN);
         st.n_kchunks = st.kind == K_STEM_IM2COL ? st.kpad / st.cb : st.kh * st.kw * (cpad / st.cb);
-        choose_pipeline(st);
+        // mode 1: stride-1 "same" convs read one halo block per tile (needs resident weights)
+        st.mode = 0;
+        if (st.kind == K_TC && cq.view_oh == 0 && st.kh == st.kw && st.kh > 1 && st.sh == 1 && st.sw == 1 &&
+            st.ph == (st.kh - 1) / 2 && st.pw == st.ph && st.ph <= 1 && st.oh == st.ih && st.ow == st.iw &&
+            st.oh * st.ow >= 64) {
+            const int wp = st.iw + 2;
+            st.blk_rows = 128 + (st.kh - 1) * wp + (st.kw - 1);
+            if (st.blk_rows <= 256) {
+                st.mode = 1;
+                st.a_stage = round_up(st.blk_rows * st.cb, 1024);
+                if (!choose_pipeline(st, 2)) st.mode = 0;
+            }
+        }
+        if (st.mode == 0) {
+            st.a_stage = 128 * st.cb;
+            choose_pipeline(st, 4);
+        }
         if (st.smem > kSmemBudget)
             return e->fail(strf("conv[%d]: no pipeline fits in shared memory", st.conv));
         if (st.kind == K_STEM_IM2COL) {
@@ -592,11 +619,23 @@ int finalize(ptq8_engine* e, int max_batch) {
             if (!make_map(e, &st.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, st.d_im2col, dims, strides, box, estr,
                           swizzle_for(st.cb)))
                 return PTQ8_ERR_CUDA;
+        } else if (st.mode == 1) {
+            const Value& vin = e->vals[st.in_val];
+            int8_t* base = vin.codes[vin.code_index(st.s_in)];
+            const cuuint64_t rows = (cuuint64_t)max_batch * (vin.h + 2) * (vin.w + 2);
+            cuuint64_t dims[2] = {(cuuint64_t)vin.c, rows};
+            cuuint64_t strides[1] = {(cuuint64_t)vin.ldq};
+            cuuint32_t box[2] = {(cuuint32_t)st.cb, (cuuint32_t)st.blk_rows};
+            cuuint32_t estr[2] = {1, 1};
+            if (!make_map(e, &st.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
+                          swizzle_for(st.cb)))
+                return PTQ8_ERR_CUDA;
         } else {
             const Value& vin = e->vals[st.in_val];
             int8_t* base = vin.codes[vin.code_index(st.s_in)];
-            cuuint64_t dims[4] = {(cuuint64_t)vin.c, (cuuint64_t)vin.w, (cuuint64_t)vin.h, (cuuint64_t)max_batch};
-            cuuint64_t strides[3] = {(cuuint64_t)vin.ldq, (cuuint64_t)vin.ldq * vin.w, (cuuint64_t)vin.ldq * vin.w * vin.h};
+            const cuuint64_t hp = vin.h + 2, wp = vin.w + 2;
+            cuuint64_t dims[4] = {(cuuint64_t)vin.c, wp, hp, (cuuint64_t)max_batch};
+            cuuint64_t strides[3] = {(cuuint64_t)vin.ldq, (cuuint64_t)vin.ldq * wp, (cuuint64_t)vin.ldq * wp * hp};
             cuuint32_t box[4] = {(cuuint32_t)st.cb, (cuuint32_t)(st.TW * st.sw), (cuuint32_t)(st.TH * st.sh),
                                  (cuuint32_t)st.TN};
             cuuint32_t estr[4] = {1, (cuuint32_t)st.sw, (cuuint32_t)st.sh, 1};
@@ -644,6 +683,11 @@ EpiParams epi_for(ptq8_engine* e, const Step& st) {
     p.out_f32 = out.need_f32 ? out.f32 : nullptr;
     p.cout = st.kind == K_MAXPOOL ? out.c : st.oc;
     p.vec32 = (p.cout % 8 == 0) ? 1 : 0;   // 32-byte aligned fp32 rows
+    if (st.conv >= 0 && e->q[st.conv].view_oh > 0) {
+        p.dcr_oc = out.c;
+        p.dcr_h = out.h;
+        p.dcr_w = out.w;
+    }
     p.act = st.act;
     p.post = st.res_val >= 0 ? st.post : 0;
     p.out_q0 = out.codes.size() > 0 ? out.codes[0] : nullptr;
@@ -691,27 +735,39 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
                                                               rows, (float)(1.0 / st.s_in), st.s_in);
     }
     ConvGeom g{};
+    g.mode = st.mode;
     g.N = n;
     g.OH = st.oh;
     g.OW = st.ow;
     g.TW = st.TW; g.TH = st.TH; g.TN = st.TN;
     g.tiles_w = (st.ow + st.TW - 1) / st.TW;
     g.tiles_h = (st.oh + st.TH - 1) / st.TH;
-    const int tiles_n = (n + st.TN - 1) / st.TN;
-    g.m_tiles = g.tiles_w * g.tiles_h * tiles_n;
+    g.KH = st.kind == K_STEM_IM2COL ? 1 : st.kh;
     if (st.kind == K_STEM_IM2COL) {
-        g.KW = 1; g.SH = 1; g.SW = 1; g.PH = 0; g.PW = 0;
+        g.KW = 1; g.KH = 1; g.SH = 1; g.SW = 1; g.PH = 0; g.PW = 0;
+        g.coord_off = 0;
         g.n_cchunks = st.kpad / st.cb;
     } else {
         g.KW = st.kw; g.SH = st.sh; g.SW = st.sw; g.PH = st.ph; g.PW = st.pw;
+        g.coord_off = 1;
         g.n_cchunks = e->vals[st.in_val].ldq / st.cb;
     }
+    if (st.mode == 1) {
+        g.Hp = st.ih + 2;
+        g.Wp = st.iw + 2;
+        g.blk_off = -(st.ph * g.Wp + st.pw);
+        g.m_tiles = (int)(((size_t)n * g.Hp * g.Wp + 127) / 128);
+        g.a_bytes = (uint32_t)(st.blk_rows * st.cb);
+    } else {
+        g.m_tiles = g.tiles_w * g.tiles_h * ((n + st.TN - 1) / st.TN);
+        g.a_bytes = (uint32_t)(st.TW * st.TH * st.TN * st.cb);
+    }
+    g.a_stage = st.a_stage;
     g.n_kchunks = st.n_kchunks;
     g.BN = st.bn;
     g.acc_cols = acc_cols_for(st.bn);
     g.stages = st.stages;
     g.b_resident = st.b_resident;
-    g.a_bytes = (uint32_t)(st.TW * st.TH * st.TN * st.cb);
     g.b_bytes = (uint32_t)(st.bn * st.cb);
     dim3 grid((unsigned)std::min(g.m_tiles, st.grid_x), (unsigned)st.n_ntiles);
     if (st.cb == 128)
@@ -1177,27 +1233,34 @@ int ptq8_engine_tensor_info(ptq8_engine* e, int what, int index, int* shape4) {
 }
 
 int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst, size_t bytes) {
-    if (!e || !e->planned || !host_dst) return PTQ8_ERR_INVALID;
+    if (!e || !e->planned || !host_dst || n <= 0 || n > e->max_batch) return PTQ8_ERR_INVALID;
     int shp[4];
     int rc = ptq8_engine_tensor_info(e, what, index, shp);
     if (rc) return rc;
-    const void* src;
-    size_t need;
+    const size_t elem = what == 0 ? 1 : sizeof(float);
+    const size_t need = (size_t)n * shp[1] * shp[2] * shp[3] * elem;
+    if (bytes < need) return e->fail("dump buffer too small");
+    if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "sync")) return PTQ8_ERR_CUDA;
     if (what == 0) {
         const Step& st = e->steps[e->conv_step[index]];
-        if (st.kind == K_STEM_IM2COL) src = st.d_im2col;
-        else {
-            const Value& v = e->vals[st.in_val];
-            src = v.codes[v.code_index(st.s_in)];
+        if (st.kind == K_STEM_IM2COL) {
+            if (!e->cuda_ok(cudaMemcpy(host_dst, st.d_im2col, need, cudaMemcpyDeviceToHost), "dump"))
+                return PTQ8_ERR_CUDA;
+            return PTQ8_OK;
         }
-        need = (size_t)n * shp[1] * shp[2] * shp[3];
-    } else {
-        src = e->vals[e->final_val].f32;
-        need = (size_t)n * shp[1] * shp[2] * shp[3] * sizeof(float);
+        const Value& v = e->vals[st.in_val];
+        const int8_t* src = v.codes[v.code_index(st.s_in)];
+        // drop the one-pixel border: per image, H rows of W*ld bytes out of (H+2) x (W+2)*ld
+        const size_t row = (size_t)v.w * v.ldq, prow = (size_t)(v.w + 2) * v.ldq;
+        for (int i = 0; i < n; ++i) {
+            const int8_t* s0 = src + ((size_t)i * (v.h + 2) + 1) * prow + v.ldq;
+            int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * v.h * row;
+            if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, v.h, cudaMemcpyDeviceToHost), "dump"))
+                return PTQ8_ERR_CUDA;
+        }
+        return PTQ8_OK;
     }
-    if (bytes < need) return e->fail("dump buffer too small");
-    if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "sync") ||
-        !e->cuda_ok(cudaMemcpy(host_dst, src, need, cudaMemcpyDeviceToHost), "dump"))
+    if (!e->cuda_ok(cudaMemcpy(host_dst, e->vals[e->final_val].f32, need, cudaMemcpyDeviceToHost), "dump"))
         return PTQ8_ERR_CUDA;
     return PTQ8_OK;
 }

@@ -62,6 +62,15 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// Arrive without release semantics.  The epilogue frees a TMEM accumulator
+// this way: the only accesses to order are its tcgen05.ld reads (completed by
+// tcgen05.wait::ld and ordered by tcgen05.fence::before_thread_sync); a release
+// arrive would also wait for the warp's outstanding global stores to reach the
+// point of coherence and put that latency on the MMA's critical path.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
+    asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -148,6 +157,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
           "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
         : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+        " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major operand tile whose rows are
@@ -205,8 +222,14 @@ __device__ __forceinline__ float acc_to_float(uint32_t acc, uint32_t& flag) {
 // Code estimate of y for scale 1/inv: nearest integer of t = y*inv clamped to
 // +-4096 (codes saturate far earlier).  *flag is raised when t lies within
 // 1e-4 of a half-integer: there the reference's float64 formula decides.
+//
+// Only the lower side needs a clamp: for t >= 2^22 the sum's exponent grows and
+// the extracted integer is a large positive number that pack4 saturates to
+// 127; whenever that happens the tie test also fails, so the exact formula
+// confirms it.  Values below -4096 are clamped (codes saturate at -128 long
+// before), which keeps the extracted integer from wrapping.
 __device__ __forceinline__ int quant_fast(float y, float inv, uint32_t& flag) {
-    const float t = fminf(fmaxf(__fmul_rn(y, inv), -4096.0f), 4096.0f);
+    const float t = fmaxf(__fmul_rn(y, inv), -4096.0f);
     const float m = __fadd_rn(t, kRoundMagic);
     flag |= fabsf(__fsub_rn(t, __fsub_rn(m, kRoundMagic))) >= 0.4999f;
     return __float_as_int(m) - kRoundMagicBits;
@@ -247,6 +270,32 @@ __device__ __forceinline__ void quant32(const float (&y)[32], float inv, double 
     }
 }
 
+__device__ __noinline__ void quant16_exact(const float* y, double s, uint32_t* w) {
+    for (int j = 0; j < 4; ++j)
+        w[j] = pack4(quant_exact(y[4 * j], s), quant_exact(y[4 * j + 1], s), quant_exact(y[4 * j + 2], s),
+                     quant_exact(y[4 * j + 3], s));
+}
+
+// 16 int8 codes of y packed into 4 words.
+__device__ __forceinline__ void quant16(const float (&y)[16], float inv, double s, uint32_t (&w)[4]) {
+    uint32_t flag = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int a = quant_fast(y[4 * j], inv, flag), b = quant_fast(y[4 * j + 1], inv, flag);
+        const int c = quant_fast(y[4 * j + 2], inv, flag), d = quant_fast(y[4 * j + 3], inv, flag);
+        w[j] = pack4(a, b, c, d);
+    }
+    if (flag) {
+        float ys[16];
+        uint32_t ws[4];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ys[j] = y[j];
+        quant16_exact(ys, s, ws);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = ws[j];
+    }
+}
+
 __device__ __forceinline__ int quant_code(float x, float inv, double s) {
     uint32_t flag = 0;
     const int q = quant_fast(x, inv, flag);
@@ -277,56 +326,69 @@ __device__ __forceinline__ float apply_act(float y, int act) {
 
 // ------------------------------------------------------------------ epilogue outputs
 
+// Layouts: fp32 activations are NHWC [N][H][W][cout]; int8 code tensors are
+// NHWC with a one-pixel zero border, [N][H+2][W+2][ldq], so that stride-1
+// convs read every tap of a tile from one contiguous block (see conv_tc_kernel).
 struct EpiParams {
     const float* factor;    // [cout] float(float(s_in) * w_scale[c])
     const float* bias;      // [cout]
     const float* residual;  // fp32 NHWC [P][cout] or null
     float* out_f32;         // fp32 NHWC [P][cout] or null
-    int8_t* out_q0;         // int8 NHWC codes [P][ldq0] or null
+    int8_t* out_q0;         // bordered int8 codes [N][OH+2][OW+2][ldq0] or null
     int8_t* out_q1;
     int ldq0, ldq1;
     float inv0, inv1;
     double s0, s1;
     int cout;
-    int vec32; // 1 when fp32 rows are 32-byte aligned (cout % 8 == 0): 256-bit loads/stores allowed
-    int act;   // activation of the conv itself: 0 none / 1 relu / 2 relu6
-    int post;  // residual: 0 none, 1 add then relu, 2 add only
+    int vec32;  // 1 when fp32 rows are 32-byte aligned (cout % 8 == 0): 256-bit loads/stores allowed
+    int act;    // activation of the conv itself: 0 none / 1 relu / 2 relu6
+    int post;   // residual: 0 none, 1 add then relu, 2 add only
+    // positional decomposition: channel c' = pos*dcr_oc + c of a 1x1 GEMM output is code
+    // (pos / dcr_w, pos % dcr_w, c) of a dcr_h x dcr_w map (DepthToSpace, DCR order)
+    int dcr_oc, dcr_h, dcr_w;
 };
 
-// Residual of 32 consecutive channels [c0, c0+32) of output position p (nv valid).
-__device__ __forceinline__ void load_res32(const EpiParams& e, size_t p, int c0, int nv, float (&r)[32]) {
-    const float* rp = e.residual + p * e.cout + c0;
-    if (nv == 32 && e.vec32) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) ld_v8(rp + j, &r[j]);
+// Residual of 16 consecutive channels [c0, c0+16) of fp32 row pf (nv valid).
+__device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0, int nv, float (&r)[16]) {
+    const float* rp = e.residual + pf * e.cout + c0;
+    if (nv == 16 && e.vec32) {
+        ld_v8(rp, &r[0]);
+        ld_v8(rp + 8, &r[8]);
     } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = j < nv ? rp[j] : 0.0f;
+        for (int j = 0; j < 16; ++j) r[j] = j < nv ? rp[j] : 0.0f;
     }
 }
 
-// Finish 32 consecutive channels [c0, c0+32) of output position p (nv of them valid):
-// residual add (values in r) + post activation, fp32 store, int8 codes per consumer scale.
-__device__ __forceinline__ void epilogue_store32(const EpiParams& e, size_t p, int c0, int nv, float (&y)[32],
-                                                 const float (&r)[32]) {
+// Finish 16 consecutive channels [c0, c0+16) (nv valid) of the output position
+// with fp32 row pf, bordered code row pq, image n: residual add (values in r)
+// + post activation, fp32 store, int8 codes per consumer scale.
+__device__ __forceinline__ void epilogue_store16(const EpiParams& e, size_t pf, size_t pq, int n, int c0, int nv,
+                                                 float (&y)[16], const float (&r)[16]) {
     if (e.post != 0) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(y[j], r[j]);
+        for (int j = 0; j < 16; ++j) y[j] = __fadd_rn(y[j], r[j]);
         if (e.post == 1) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = fmaxf(y[j], 0.0f);
+            for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.0f);
         }
     }
     if (e.out_f32) {
-        float* op = e.out_f32 + p * e.cout + c0;
-        if (nv == 32 && e.vec32) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) st_v8(op + j, &y[j]);
+        float* op = e.out_f32 + pf * e.cout + c0;
+        if (nv == 16 && e.vec32) {
+            st_v8(op, &y[0]);
+            st_v8(op + 8, &y[8]);
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
+            for (int j = 0; j < 16; ++j)
                 if (j < nv) op[j] = y[j];
         }
+    }
+    int cq = c0;
+    if (e.dcr_oc) {
+        const int pos = c0 / e.dcr_oc;
+        cq = c0 - pos * e.dcr_oc;
+        pq = (static_cast<size_t>(n) * (e.dcr_h + 2) + pos / e.dcr_w + 1) * (e.dcr_w + 2) + pos % e.dcr_w + 1;
     }
 #pragma unroll
     for (int o = 0; o < 2; ++o) {
@@ -334,14 +396,14 @@ __device__ __forceinline__ void epilogue_store32(const EpiParams& e, size_t p, i
         if (!qbase) continue;
         const float inv = o == 0 ? e.inv0 : e.inv1;
         const double s = o == 0 ? e.s0 : e.s1;
-        int8_t* qp = qbase + p * static_cast<size_t>(o == 0 ? e.ldq0 : e.ldq1) + c0;
-        if (nv == 32) {
-            uint32_t w[8];
-            quant32(y, inv, s, w);
-            st_v8(reinterpret_cast<uint32_t*>(qp), w);
+        int8_t* qp = qbase + pq * static_cast<size_t>(o == 0 ? e.ldq0 : e.ldq1) + cq;
+        if (nv == 16) {
+            uint32_t w[4];
+            quant16(y, inv, s, w);
+            *reinterpret_cast<uint4*>(qp) = make_uint4(w[0], w[1], w[2], w[3]);
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
+            for (int j = 0; j < 16; ++j)
                 if (j < nv) qp[j] = sat8(quant_code(y[j], inv, s));
         }
     }
@@ -350,11 +412,18 @@ __device__ __forceinline__ void epilogue_store32(const EpiParams& e, size_t p, i
 // ------------------------------------------------------------------ tensor-core conv
 
 struct ConvGeom {
+    int mode;                   // 0: per-tap 4-D tile loads; 1: one halo block per tile, taps = shifted views
     int N, OH, OW;              // output map (per image)
+    // mode 0
     int TW, TH, TN;             // one M tile = TN images x TH rows x TW cols (<= 128 positions)
     int tiles_w, tiles_h;       // M tiles along W and H
-    int m_tiles;                // total M tiles
     int KW, SH, SW, PH, PW;     // kernel width, strides, paddings
+    int coord_off;              // 1 when the A tensor carries the one-pixel border
+    // mode 1 (stride 1, same-size output): tiles are 128 consecutive bordered positions
+    int KH, Hp, Wp;             // kernel height, bordered map dims
+    int blk_off;                // first block row relative to the tile's first row
+    int a_stage;                // bytes per A stage (1024-aligned)
+    int m_tiles;                // total M tiles
     int n_cchunks, n_kchunks;   // channel chunks per tap, total K chunks
     int BN;                     // N tile (multiple of 16, <= 256)
     int acc_cols;               // TMEM columns per accumulator buffer (power of two >= max(32, BN))
@@ -363,13 +432,20 @@ struct ConvGeom {
     uint32_t a_bytes, b_bytes;  // TMA bytes per A stage / per B chunk
 };
 
-constexpr int kConvThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;                      // 4 per TMEM lane quadrant
+constexpr int kConvThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int kMaxStages = 24;
 
 // Persistent implicit-GEMM conv.  grid = (CTAs per N tile, N tiles); each CTA
 // walks M tiles blockIdx.x, blockIdx.x + gridDim.x, ...  Two TMEM accumulators
 // let the epilogue of tile i overlap the MMAs of tile i+1.
+//
+// mode 0: every K chunk (tap, channel chunk) is its own 4-D TMA box of the
+//         input (element strides give stride 2; out-of-range boxes read zeros).
+// mode 1: a tile is 128 consecutive positions of the bordered map; one 2-D box
+//         of 128 + (KH-1)*Wp + KW-1 bordered rows per channel chunk holds every
+//         tap, and tap (i, j) is the same shared-memory block seen from row
+//         i*Wp + j.  Border outputs are computed and dropped.
 template <int CB>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -389,7 +465,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int S = g.stages;
     const int sb_stride = (BN * CB + 1023) & ~1023;   // every B chunk 1024-byte aligned (swizzle atoms)
     uint8_t* sA = smem;
-    uint8_t* sB = smem + S * 128 * CB;
+    uint8_t* sB = smem + S * g.a_stage;
     float* s_factor = reinterpret_cast<float*>(sB + (g.b_resident ? g.n_kchunks : S) * sb_stride);
     float* s_bias = s_factor + bn32;
 
@@ -434,6 +510,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    const int n_a = g.mode == 1 ? g.n_cchunks : g.n_kchunks;   // A loads per tile
 
     if (warp == 0) {
         if (lane == 0) {
@@ -449,25 +526,32 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             int s = 0;
             uint32_t ph = 0;
             for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
-                const int tw_i = mt % g.tiles_w;
-                const int rest = mt / g.tiles_w;
-                const int th_i = rest % g.tiles_h;
-                const int tn_i = rest / g.tiles_h;
-                const int w0 = tw_i * g.TW, h0 = th_i * g.TH, n0 = tn_i * g.TN;
+                int w0 = 0, h0 = 0, n0 = 0;
+                if (g.mode == 0) {
+                    const int tw_i = mt % g.tiles_w;
+                    const int rest = mt / g.tiles_w;
+                    w0 = tw_i * g.TW;
+                    h0 = (rest % g.tiles_h) * g.TH;
+                    n0 = (rest / g.tiles_h) * g.TN;
+                }
                 int tap = 0, cc = 0;
-                for (int kc = 0; kc < g.n_kchunks; ++kc) {
+                for (int ka = 0; ka < n_a; ++ka) {
                     if (!mbar_wait(empty0 + 8 * s, ph ^ 1)) {
                         atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
                         ok = false;
                         break;
                     }
-                    const int ki = tap / g.KW;
-                    const int kj = tap - ki * g.KW;
                     const uint32_t fb = full0 + 8 * s;
                     mbar_expect_tx(fb, g.a_bytes + (g.b_resident ? 0u : g.b_bytes));
-                    tma_load_4d(smem_u32(sA + s * 128 * CB), &map_a, fb, cc * CB, w0 * g.SW + kj - g.PW,
-                                h0 * g.SH + ki - g.PH, n0);
-                    if (!g.b_resident) tma_load_2d(smem_u32(sB + s * sb_stride), &map_b, fb, kc * CB, nt * BN);
+                    if (g.mode == 1) {
+                        tma_load_2d(smem_u32(sA + s * g.a_stage), &map_a, fb, ka * CB, mt * 128 + g.blk_off);
+                    } else {
+                        const int ki = tap / g.KW;
+                        const int kj = tap - ki * g.KW;
+                        tma_load_4d(smem_u32(sA + s * g.a_stage), &map_a, fb, cc * CB,
+                                    w0 * g.SW + kj - g.PW + g.coord_off, h0 * g.SH + ki - g.PH + g.coord_off, n0);
+                        if (!g.b_resident) tma_load_2d(smem_u32(sB + s * sb_stride), &map_b, fb, ka * CB, nt * BN);
+                    }
                     last_ph = (last_ph & ~(1u << s)) | (ph << s);
                     used |= 1u << s;
                     if (++cc == g.n_cchunks) { cc = 0; ++tap; }
@@ -487,6 +571,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (lane == 0) {
             // ---------------- MMA issuer
             const uint32_t idesc = make_idesc_i8(BN);
+            const int taps = g.KH * g.KW;
+            // descriptors of stage 0 / B chunk 0; other stages, taps and chunks only move the start address
+            const uint64_t adesc0 = make_sdesc(smem_u32(sA), CB);
+            const uint64_t bdesc0 = make_sdesc(smem_u32(sB), CB);
+            int tap_off[25];   // mode 1: start of tap (i, j) in 16-byte units
+            for (int tap = 0; tap < taps && tap < 25; ++tap)
+                tap_off[tap] = ((tap / g.KW) * g.Wp + tap % g.KW) * CB >> 4;
             bool ok = !g.b_resident || mbar_wait(bfull, 0);
             if (!ok) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
             int s = 0;
@@ -501,19 +592,28 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + static_cast<uint32_t>(buf * g.acc_cols);
-                for (int kc = 0; kc < g.n_kchunks; ++kc) {
+                for (int ka = 0; ka < n_a; ++ka) {
                     if (!mbar_wait(full0 + 8 * s, ph)) {
                         atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t da = make_sdesc(smem_u32(sA + s * 128 * CB), CB);
-                    const uint64_t db =
-                        make_sdesc(smem_u32(sB + (g.b_resident ? kc : s) * sb_stride), CB);
+                    const uint64_t da0 = adesc0 + static_cast<uint64_t>((s * g.a_stage) >> 4);
+                    if (g.mode == 1) {
+                        for (int tap = 0; tap < taps; ++tap) {
+                            const uint64_t da = da0 + static_cast<uint64_t>(tap_off[tap]);
+                            const uint64_t db = bdesc0 + static_cast<uint64_t>(((tap * g.n_cchunks + ka) * sb_stride) >> 4);
 #pragma unroll
-                    for (int k = 0; k < CB / 32; ++k)
-                        mma_i8(d, da + 2 * k, db + 2 * k, idesc, (kc | k) != 0 ? 1u : 0u);
+                            for (int k = 0; k < CB / 32; ++k)
+                                mma_i8(d, da + 2 * k, db + 2 * k, idesc, (ka | tap | k) != 0 ? 1u : 0u);
+                        }
+                    } else {
+                        const uint64_t db = bdesc0 + static_cast<uint64_t>(((g.b_resident ? ka : s) * sb_stride) >> 4);
+#pragma unroll
+                        for (int k = 0; k < CB / 32; ++k)
+                            mma_i8(d, da0 + 2 * k, db + 2 * k, idesc, (ka | k) != 0 ? 1u : 0u);
+                    }
                     mma_commit(empty0 + 8 * s);
                     if (++s == S) { s = 0; ph ^= 1; }
                 }
@@ -525,73 +625,83 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             if (!mbar_wait(donebar, 0)) atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
         }
     } else {
-        // ---------------- epilogue: TMEM lanes 32*(warp%4) .. +31 = tile rows
+        // ---------------- epilogue: TMEM lanes 32*(warp%4) .. +31 = tile rows;
+        // the kEpiWarps/4 warps of a quadrant take interleaved 16-column groups
         const int quad = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int slice = (warp - 2) >> 2;
+        constexpr int kSlices = kEpiWarps / 4;
         const int r = quad * 32 + lane;
         const int tw = g.TW, th = g.TH;
         const int rn = r / (tw * th), rh = (r / tw) % th, rw = r % tw;
         const bool in_tile = r < tw * th * g.TN;
         const int tile_end = min(e.cout, (nt + 1) * BN);
-        const int ncg = bn32 / 32;
+        const int ncg = bn32 / 16;
         int t = 0;
         for (int mt = blockIdx.x; mt < g.m_tiles; mt += gridDim.x, ++t) {
             const int buf = t & 1;
             const uint32_t use = static_cast<uint32_t>(t >> 1);
-            const int tw_i = mt % g.tiles_w;
-            const int rest = mt / g.tiles_w;
-            const int th_i = rest % g.tiles_h;
-            const int tn_i = rest / g.tiles_h;
-            const int n = tn_i * g.TN + rn, h = th_i * g.TH + rh, w = tw_i * g.TW + rw;
-            const bool valid = in_tile && n < g.N && h < g.OH && w < g.OW;
-            const size_t p = (static_cast<size_t>(n) * g.OH + h) * g.OW + w;
+            int n, h, w;
+            bool valid;
+            size_t pq;
+            if (g.mode == 1) {
+                const size_t q = static_cast<size_t>(mt) * 128 + r;
+                const size_t img = static_cast<size_t>(g.Hp) * g.Wp;
+                n = static_cast<int>(q / img);
+                const int rem = static_cast<int>(q - static_cast<size_t>(n) * img);
+                h = rem / g.Wp - 1;
+                w = rem - (rem / g.Wp) * g.Wp - 1;
+                valid = n < g.N && h >= 0 && h < g.OH && w >= 0 && w < g.OW;
+                pq = q;
+            } else {
+                const int tw_i = mt % g.tiles_w;
+                const int rest = mt / g.tiles_w;
+                n = (rest / g.tiles_h) * g.TN + rn;
+                h = (rest % g.tiles_h) * g.TH + rh;
+                w = tw_i * g.TW + rw;
+                valid = in_tile && n < g.N && h < g.OH && w < g.OW;
+                pq = (static_cast<size_t>(n) * (g.OH + 2) + h + 1) * (g.OW + 2) + w + 1;
+            }
+            const size_t pf = (static_cast<size_t>(n) * g.OH + h) * g.OW + w;
             // the residual does not depend on the MMAs: fetch the first group before waiting
-            float res[32];
+            float res[16];
             {
-                const int c0 = nt * BN + half * 32;
-                if (e.post != 0 && valid && half < ncg && c0 < tile_end) load_res32(e, p, c0, min(32, tile_end - c0), res);
+                const int c0 = nt * BN + slice * 16;
+                if (e.post != 0 && valid && slice < ncg && c0 < tile_end) load_res16(e, pf, c0, min(16, tile_end - c0), res);
             }
             if (!mbar_wait(accf0 + 8 * buf, use & 1u)) {
                 atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
                 break;
             }
             tc_fence_after();
-            for (int cg = half; cg < ncg; cg += 2) {
-                uint32_t v[32];
+            for (int cg = slice; cg < ncg; cg += kSlices) {
+                uint32_t v[16];
                 __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the per-lane stores
-                tmem_ld32(tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16) +
-                              cg * 32,
+                tmem_ld16(tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16) +
+                              cg * 16,
                           v);
                 tmem_wait_ld();
-                const int c0 = nt * BN + cg * 32;
+                const int c0 = nt * BN + cg * 16;
                 if (!valid || c0 >= tile_end) continue;
-                const int nv = min(32, tile_end - c0);
-                float y[32];
-                const float4* f4 = reinterpret_cast<const float4*>(s_factor + cg * 32);
-                const float4* b4 = reinterpret_cast<const float4*>(s_bias + cg * 32);
-                uint32_t big = 0;
+                const int nv = min(16, tile_end - c0);
+                float y[16];
+                const float4* f4 = reinterpret_cast<const float4*>(s_factor + cg * 16);
+                const float4* b4 = reinterpret_cast<const float4*>(s_bias + cg * 16);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) y[j] = acc_to_float(v[j], big);
-                if (big) {   // |acc| >= 2^22 somewhere: convert with the rounding instruction
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) y[j] = __int2float_rn(static_cast<int>(v[j]));
-                }
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < 4; ++j) {
                     const float4 f = f4[j], bb = b4[j];
-                    y[4 * j + 0] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 0], f.x), bb.x), e.act);
-                    y[4 * j + 1] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 1], f.y), bb.y), e.act);
-                    y[4 * j + 2] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 2], f.z), bb.z), e.act);
-                    y[4 * j + 3] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 3], f.w), bb.w), e.act);
+                    y[4 * j + 0] = apply_act(__fadd_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[4 * j + 0])), f.x), bb.x), e.act);
+                    y[4 * j + 1] = apply_act(__fadd_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[4 * j + 1])), f.y), bb.y), e.act);
+                    y[4 * j + 2] = apply_act(__fadd_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[4 * j + 2])), f.z), bb.z), e.act);
+                    y[4 * j + 3] = apply_act(__fadd_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[4 * j + 3])), f.w), bb.w), e.act);
                 }
-                epilogue_store32(e, p, c0, nv, y, res);
+                epilogue_store16(e, pf, pq, n, c0, nv, y, res);
                 // prefetch the residual of this warp's next column group
-                const int cn = c0 + 64;
-                if (e.post != 0 && cg + 2 < ncg && cn < tile_end) load_res32(e, p, cn, min(32, tile_end - cn), res);
+                const int cn = c0 + 16 * kSlices;
+                if (e.post != 0 && cg + kSlices < ncg && cn < tile_end) load_res16(e, pf, cn, min(16, tile_end - cn), res);
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acce0 + 8 * buf);
+            if (lane == 0) mbar_arrive_relaxed(acce0 + 8 * buf);
         }
     }
     tc_fence_before();
@@ -653,9 +763,9 @@ __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restri
 
 // ------------------------------------------------------------------ depthwise conv
 
-// Depthwise kxk conv over int8 NHWC codes [N][H][W][ldi] (C channels), int32
-// accumulation, then the shared exact epilogue.  One thread per (position,
-// 4 channels); weights w[tap][C] int8.
+// Depthwise kxk conv over bordered int8 codes [N][H+2][W+2][ldi] (C channels),
+// int32 accumulation, then the shared exact epilogue.  One thread per
+// (position, 4 channels); weights w[tap][C] int8.
 __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int8_t* __restrict__ w, int N, int H,
                                int W, int C, int OH, int OW, int KH, int KW, int SH, int SW, int PH, int PW,
                                const EpiParams e) {
@@ -676,7 +786,8 @@ __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int
             for (int j = 0; j < KW; ++j) {
                 const int iw = ow * SW + j - PW;
                 if (iw < 0 || iw >= W) continue;
-                const char4 xv = *reinterpret_cast<const char4*>(in + ((static_cast<size_t>(n) * H + ih) * W + iw) * ldi + c0);
+                const char4 xv = *reinterpret_cast<const char4*>(
+                    in + ((static_cast<size_t>(n) * (H + 2) + ih + 1) * (W + 2) + iw + 1) * ldi + c0);
                 const int8_t* wr = w + static_cast<size_t>(i * KW + j) * C + c0;
                 acc[0] += static_cast<int>(xv.x) * wr[0];
                 if (c0 + 1 < C) acc[1] += static_cast<int>(xv.y) * wr[1];
@@ -699,17 +810,18 @@ __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int
         }
         if (e.out_f32)
             for (int b = 0; b < nv; ++b) e.out_f32[p * C + c0 + b] = y[b];
+        const size_t pq = (static_cast<size_t>(n) * (OH + 2) + oh + 1) * (OW + 2) + ow + 1;
         if (e.out_q0)
-            for (int b = 0; b < nv; ++b) e.out_q0[p * e.ldq0 + c0 + b] = sat8(quant_code(y[b], e.inv0, e.s0));
+            for (int b = 0; b < nv; ++b) e.out_q0[pq * e.ldq0 + c0 + b] = sat8(quant_code(y[b], e.inv0, e.s0));
         if (e.out_q1)
-            for (int b = 0; b < nv; ++b) e.out_q1[p * e.ldq1 + c0 + b] = sat8(quant_code(y[b], e.inv1, e.s1));
+            for (int b = 0; b < nv; ++b) e.out_q1[pq * e.ldq1 + c0 + b] = sat8(quant_code(y[b], e.inv1, e.s1));
     }
 }
 
 // ------------------------------------------------------------------ stem maxpool
 
 // 3x3/s2/p1 maxpool (padding never wins) of fp32 NHWC [N][H][W][C]; writes the
-// pooled fp32 map and its codes.  Quantization is monotone, so pooling the fp32
+// pooled fp32 map and its (bordered) codes.  Quantization is monotone, so pooling the fp32
 // values and then quantizing equals the reference's order (ref_e2e.py:192-203).
 __global__ void maxpool_kernel(const float* __restrict__ in, int N, int H, int W, int C, int OH, int OW,
                                const EpiParams e) {
@@ -732,8 +844,9 @@ __global__ void maxpool_kernel(const float* __restrict__ in, int N, int H, int W
             }
         }
         if (e.out_f32) e.out_f32[p * C + c] = m;
-        if (e.out_q0) e.out_q0[p * e.ldq0 + c] = sat8(quant_code(m, e.inv0, e.s0));
-        if (e.out_q1) e.out_q1[p * e.ldq1 + c] = sat8(quant_code(m, e.inv1, e.s1));
+        const size_t pq = (static_cast<size_t>(n) * (OH + 2) + oh + 1) * (OW + 2) + ow + 1;
+        if (e.out_q0) e.out_q0[pq * e.ldq0 + c] = sat8(quant_code(m, e.inv0, e.s0));
+        if (e.out_q1) e.out_q1[pq * e.ldq1 + c] = sat8(quant_code(m, e.inv1, e.s1));
     }
 }
 
