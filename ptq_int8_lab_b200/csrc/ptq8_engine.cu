@@ -93,6 +93,7 @@ struct Step {
     int a_stage = 0;       // bytes per A pipeline stage
     size_t smem = 0;
     int grid_x = 1;
+    void* kfn = nullptr;   // conv_tc_kernel specialization
     int TW = 1, TH = 1, TN = 1;
     double s_in = 1.0;
     // device parameters
@@ -446,6 +447,33 @@ bool make_map(ptq8_engine* e, CUtensorMap* map, CUtensorMapDataType dt, int rank
 
 constexpr size_t kSmemBudget = 225 * 1024;
 
+// conv_tc_kernel specializations: [K-chunk 32/64/128][mode][code outputs][residual][fp32 out]
+void* g_conv_table[3][2][3][2][2];
+
+template <int CBI, int MODE, int NOUT, int RES, int F32>
+void fill_one() {
+    g_conv_table[CBI][MODE][NOUT][RES][F32] =
+        reinterpret_cast<void*>(&conv_tc_kernel<(32 << CBI), MODE, NOUT, RES != 0, F32 != 0>);
+}
+template <int CBI, int MODE, int NOUT, int RES>
+void fill_f32() { fill_one<CBI, MODE, NOUT, RES, 0>(); fill_one<CBI, MODE, NOUT, RES, 1>(); }
+template <int CBI, int MODE, int NOUT>
+void fill_res() { fill_f32<CBI, MODE, NOUT, 0>(); fill_f32<CBI, MODE, NOUT, 1>(); }
+template <int CBI, int MODE>
+void fill_nout() { fill_res<CBI, MODE, 0>(); fill_res<CBI, MODE, 1>(); fill_res<CBI, MODE, 2>(); }
+template <int CBI>
+void fill_mode() { fill_nout<CBI, 0>(); fill_nout<CBI, 1>(); }
+void fill_table() {
+    static bool done = false;
+    if (done) return;
+    fill_mode<0>();
+    fill_mode<1>();
+    fill_mode<2>();
+    done = true;
+}
+
+int cb_index(int cb) { return cb == 128 ? 2 : (cb == 64 ? 1 : 0); }
+
 // Dynamic shared memory of conv_tc_kernel for a pipeline shape.
 size_t conv_smem_bytes(int a_stage, int cb, int bn, int stages, int b_chunks) {
     const size_t sb = (size_t)round_up(bn * cb, 1024);
@@ -488,6 +516,9 @@ int acc_cols_for(int bn) {
     while (tc < bn) tc <<= 1;
     return tc;
 }
+
+// Accumulator buffers in TMEM (512 columns): 4 when they fit, else 2.
+int n_acc_for(int bn) { return 4 * acc_cols_for(bn) <= 512 ? 4 : 2; }
 
 int finalize(ptq8_engine* e, int max_batch) {
     const Model& m = *e->model;
@@ -647,20 +678,22 @@ int finalize(ptq8_engine* e, int max_batch) {
         }
     }
     {
-        const int mx = (int)kSmemBudget;
-        if (!e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr") ||
-            !e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr") ||
-            !e->cuda_ok(cudaFuncSetAttribute(conv_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx), "smem attr"))
-            return PTQ8_ERR_CUDA;
+        fill_table();
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, e->device);
         for (Step& st : e->steps) {
             if (st.kind != K_TC && st.kind != K_STEM_IM2COL) continue;
+            const Value& out = e->vals[st.out_val];
+            const int nout = (int)out.scales.size();
+            const int res = st.res_val >= 0 ? 1 : 0;
+            const int f32 = out.need_f32 ? 1 : 0;
+            st.kfn = g_conv_table[cb_index(st.cb)][st.mode][nout][res][f32];
+            if (!e->cuda_ok(cudaFuncSetAttribute(st.kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget),
+                            "smem attr"))
+                return PTQ8_ERR_CUDA;
             int occ = 1;
-            if (st.cb == 128) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, conv_tc_kernel<128>, kConvThreads, st.smem);
-            else if (st.cb == 64) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, conv_tc_kernel<64>, kConvThreads, st.smem);
-            else cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, conv_tc_kernel<32>, kConvThreads, st.smem);
-            const int occ_tmem = 512 / (2 * acc_cols_for(st.bn));
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, st.kfn, kConvThreads, st.smem);
+            const int occ_tmem = 512 / (n_acc_for(st.bn) * acc_cols_for(st.bn));
             occ = std::max(1, std::min(occ, occ_tmem));
             st.grid_x = std::max(1, sms * occ / st.n_ntiles);
         }
@@ -766,16 +799,14 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.n_kchunks = st.n_kchunks;
     g.BN = st.bn;
     g.acc_cols = acc_cols_for(st.bn);
+    g.n_acc = n_acc_for(st.bn);
     g.stages = st.stages;
     g.b_resident = st.b_resident;
     g.b_bytes = (uint32_t)(st.bn * st.cb);
     dim3 grid((unsigned)std::min(g.m_tiles, st.grid_x), (unsigned)st.n_ntiles);
-    if (st.cb == 128)
-        conv_tc_kernel<128><<<grid, kConvThreads, st.smem, s>>>(st.map_a, st.map_b, g, ep);
-    else if (st.cb == 64)
-        conv_tc_kernel<64><<<grid, kConvThreads, st.smem, s>>>(st.map_a, st.map_b, g, ep);
-    else
-        conv_tc_kernel<32><<<grid, kConvThreads, st.smem, s>>>(st.map_a, st.map_b, g, ep);
+    CUtensorMap ma = st.map_a, mb = st.map_b;
+    void* args[4] = {&ma, &mb, &g, &ep};
+    cudaLaunchKernel(st.kfn, grid, dim3(kConvThreads), args, st.smem, s);
 }
 
 int enqueue(ptq8_engine* e, int n) {

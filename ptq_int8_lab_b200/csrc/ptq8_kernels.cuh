@@ -360,12 +360,34 @@ __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0
     }
 }
 
-// Finish 16 consecutive channels [c0, c0+16) (nv valid) of the output position
-// with fp32 row pf, bordered code row pq, image n: residual add (values in r)
-// + post activation, fp32 store, int8 codes per consumer scale.
-__device__ __forceinline__ void epilogue_store16(const EpiParams& e, size_t pf, size_t pq, int n, int c0, int nv,
-                                                 float (&y)[16], const float (&r)[16]) {
-    if (e.post != 0) {
+// Dequantize 16 accumulators of channels [c, c+16) (factor/bias from shared
+// memory): y = act(fadd(fmul(float(acc), factor), bias)), two roundings.
+__device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float* sf, const float* sb, int act,
+                                          float (&y)[16]) {
+    uint32_t big = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = acc_to_float(v[j], big);
+    if (big) {   // |acc| >= 2^22 somewhere: convert with the rounding instruction
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = __int2float_rn(static_cast<int>(v[j]));
+    }
+    const float4* f4 = reinterpret_cast<const float4*>(sf);
+    const float4* b4 = reinterpret_cast<const float4*>(sb);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float4 f = f4[j], bb = b4[j];
+        y[4 * j + 0] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 0], f.x), bb.x), act);
+        y[4 * j + 1] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 1], f.y), bb.y), act);
+        y[4 * j + 2] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 2], f.z), bb.z), act);
+        y[4 * j + 3] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 3], f.w), bb.w), act);
+    }
+}
+
+// Residual add + post activation and the fp32 store of 16 channels [c0, c0+16) (nv valid).
+template <bool RES, bool F32>
+__device__ __forceinline__ void finish16(const EpiParams& e, size_t pf, int c0, int nv, float (&y)[16],
+                                         const float (&r)[16]) {
+    if constexpr (RES) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] = __fadd_rn(y[j], r[j]);
         if (e.post == 1) {
@@ -373,7 +395,7 @@ __device__ __forceinline__ void epilogue_store16(const EpiParams& e, size_t pf, 
             for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.0f);
         }
     }
-    if (e.out_f32) {
+    if constexpr (F32) {
         float* op = e.out_f32 + pf * e.cout + c0;
         if (nv == 16 && e.vec32) {
             st_v8(op, &y[0]);
@@ -384,29 +406,17 @@ __device__ __forceinline__ void epilogue_store16(const EpiParams& e, size_t pf, 
                 if (j < nv) op[j] = y[j];
         }
     }
+}
+
+// Code row of output o for channel c0 (bordered layout; positional decomposition remaps).
+__device__ __forceinline__ int8_t* code_ptr(const EpiParams& e, int o, size_t pq, int n, int c0) {
     int cq = c0;
     if (e.dcr_oc) {
         const int pos = c0 / e.dcr_oc;
         cq = c0 - pos * e.dcr_oc;
         pq = (static_cast<size_t>(n) * (e.dcr_h + 2) + pos / e.dcr_w + 1) * (e.dcr_w + 2) + pos % e.dcr_w + 1;
     }
-#pragma unroll
-    for (int o = 0; o < 2; ++o) {
-        int8_t* qbase = o == 0 ? e.out_q0 : e.out_q1;
-        if (!qbase) continue;
-        const float inv = o == 0 ? e.inv0 : e.inv1;
-        const double s = o == 0 ? e.s0 : e.s1;
-        int8_t* qp = qbase + pq * static_cast<size_t>(o == 0 ? e.ldq0 : e.ldq1) + cq;
-        if (nv == 16) {
-            uint32_t w[4];
-            quant16(y, inv, s, w);
-            *reinterpret_cast<uint4*>(qp) = make_uint4(w[0], w[1], w[2], w[3]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (j < nv) qp[j] = sat8(quant_code(y[j], inv, s));
-        }
-    }
+    return (o == 0 ? e.out_q0 : e.out_q1) + pq * static_cast<size_t>(o == 0 ? e.ldq0 : e.ldq1) + cq;
 }
 
 // ------------------------------------------------------------------ tensor-core conv
@@ -427,6 +437,7 @@ struct ConvGeom {
     int n_cchunks, n_kchunks;   // channel chunks per tap, total K chunks
     int BN;                     // N tile (multiple of 16, <= 256)
     int acc_cols;               // TMEM columns per accumulator buffer (power of two >= max(32, BN))
+    int n_acc;                  // accumulator buffers (2 or 4): tiles in flight between MMA and epilogue
     int stages;                 // A (and streamed B) pipeline depth, <= kMaxStages
     int b_resident;             // 1: the CTA's whole weight slab stays in shared memory
     uint32_t a_bytes, b_bytes;  // TMA bytes per A stage / per B chunk
@@ -446,13 +457,16 @@ constexpr int kMaxStages = 24;
 //         of 128 + (KH-1)*Wp + KW-1 bordered rows per channel chunk holds every
 //         tap, and tap (i, j) is the same shared-memory block seen from row
 //         i*Wp + j.  Border outputs are computed and dropped.
-template <int CB>
+// Template parameters fix the per-launch shape of the work so each launch runs
+// a lean instruction stream: CB = K-chunk bytes (swizzle width), MODE (above),
+// NOUT = int8 code outputs (0..2), RES = residual add, F32 = fp32 output.
+template <int CB, int MODE, int NOUT, bool RES, bool F32>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const ConvGeom g, const EpiParams e) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_abort;
-    __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 6];   // a_full, a_empty, b_full, acc_full[2], acc_empty[2], done
+    __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 10];  // a_full, a_empty, b_full, acc_full[4], acc_empty[4], done
     __shared__ uint32_t tslot;
     // A wait of an earlier CTA already ran out: skip the work (block-uniform decision).
     if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile int*>(&g_ptq8_error);
@@ -476,8 +490,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const uint32_t empty0 = smem_u32(&bars[kMaxStages]);
     const uint32_t bfull = smem_u32(&bars[2 * kMaxStages]);
     const uint32_t accf0 = smem_u32(&bars[2 * kMaxStages + 1]);
-    const uint32_t acce0 = smem_u32(&bars[2 * kMaxStages + 3]);
-    const uint32_t donebar = smem_u32(&bars[2 * kMaxStages + 5]);
+    const uint32_t acce0 = smem_u32(&bars[2 * kMaxStages + 5]);
+    const uint32_t donebar = smem_u32(&bars[2 * kMaxStages + 9]);
+    const int NA = g.n_acc;
+    const int group_warps = kEpiWarps / NA;   // epilogue warps per accumulator buffer (multiple of 4)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -485,17 +501,17 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             mbar_init(empty0 + 8 * s, 1);
         }
         mbar_init(bfull, 1);
-        mbar_init(accf0, 1);
-        mbar_init(accf0 + 8, 1);
-        mbar_init(acce0, kEpiWarps);
-        mbar_init(acce0 + 8, kEpiWarps);
+        for (int b = 0; b < NA; ++b) {
+            mbar_init(accf0 + 8 * b, 1);
+            mbar_init(acce0 + 8 * b, group_warps);
+        }
         mbar_init(donebar, 1);
         fence_mbar_init();
         tma_prefetch(&map_a);
         tma_prefetch(&map_b);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(&tslot), 2 * g.acc_cols);
+        tmem_alloc(smem_u32(&tslot), NA * g.acc_cols);
         tmem_relinquish();
     }
     if (warp >= 2) {
@@ -510,7 +526,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
-    const int n_a = g.mode == 1 ? g.n_cchunks : g.n_kchunks;   // A loads per tile
+    const int n_a = MODE == 1 ? g.n_cchunks : g.n_kchunks;   // A loads per tile
 
     if (warp == 0) {
         if (lane == 0) {
@@ -543,7 +559,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     }
                     const uint32_t fb = full0 + 8 * s;
                     mbar_expect_tx(fb, g.a_bytes + (g.b_resident ? 0u : g.b_bytes));
-                    if (g.mode == 1) {
+                    if (MODE == 1) {
                         tma_load_2d(smem_u32(sA + s * g.a_stage), &map_a, fb, ka * CB, mt * 128 + g.blk_off);
                     } else {
                         const int ki = tap / g.KW;
@@ -571,21 +587,23 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (lane == 0) {
             // ---------------- MMA issuer
             const uint32_t idesc = make_idesc_i8(BN);
-            const int taps = g.KH * g.KW;
-            // descriptors of stage 0 / B chunk 0; other stages, taps and chunks only move the start address
+            // descriptors of stage 0 / B chunk 0; other stages, taps and chunks only move the
+            // start address (16-byte units).  The issue loop is kept to register adds: the
+            // tensor core takes small MMAs as fast as this thread can issue them.
             const uint64_t adesc0 = make_sdesc(smem_u32(sA), CB);
             const uint64_t bdesc0 = make_sdesc(smem_u32(sB), CB);
-            int tap_off[25];   // mode 1: start of tap (i, j) in 16-byte units
-            for (int tap = 0; tap < taps && tap < 25; ++tap)
-                tap_off[tap] = ((tap / g.KW) * g.Wp + tap % g.KW) * CB >> 4;
+            const uint64_t a_row_step = static_cast<uint64_t>((g.Wp * CB) >> 4);      // mode 1: next kernel row
+            const uint64_t b_tap_step = static_cast<uint64_t>((g.n_cchunks * sb_stride) >> 4);
+            const uint64_t a_stage_step = static_cast<uint64_t>(g.a_stage >> 4);
+            const uint64_t b_chunk_step = static_cast<uint64_t>(sb_stride >> 4);
             bool ok = !g.b_resident || mbar_wait(bfull, 0);
             if (!ok) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
             int s = 0;
             uint32_t ph = 0;
             int t = 0;
             for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x, ++t) {
-                const int buf = t & 1;
-                const uint32_t use = static_cast<uint32_t>(t >> 1);
+                const int buf = t % NA;
+                const uint32_t use = static_cast<uint32_t>(t / NA);
                 if (!mbar_wait(acce0 + 8 * buf, (use & 1u) ^ 1u)) {
                     atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
                     break;
@@ -599,17 +617,23 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t da0 = adesc0 + static_cast<uint64_t>((s * g.a_stage) >> 4);
-                    if (g.mode == 1) {
-                        for (int tap = 0; tap < taps; ++tap) {
-                            const uint64_t da = da0 + static_cast<uint64_t>(tap_off[tap]);
-                            const uint64_t db = bdesc0 + static_cast<uint64_t>(((tap * g.n_cchunks + ka) * sb_stride) >> 4);
+                    const uint64_t da0 = adesc0 + static_cast<uint64_t>(s) * a_stage_step;
+                    if (MODE == 1) {
+                        uint64_t da_row = da0;
+                        uint64_t db = bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step;
+                        uint32_t acc = ka != 0 ? 1u : 0u;
+                        for (int i = 0; i < g.KH; ++i, da_row += a_row_step) {
+                            uint64_t da = da_row;
+                            for (int j = 0; j < g.KW; ++j, da += static_cast<uint64_t>(CB >> 4), db += b_tap_step) {
 #pragma unroll
-                            for (int k = 0; k < CB / 32; ++k)
-                                mma_i8(d, da + 2 * k, db + 2 * k, idesc, (ka | tap | k) != 0 ? 1u : 0u);
+                                for (int k = 0; k < CB / 32; ++k) {
+                                    mma_i8(d, da + 2 * k, db + 2 * k, idesc, acc);
+                                    acc = 1u;
+                                }
+                            }
                         }
                     } else {
-                        const uint64_t db = bdesc0 + static_cast<uint64_t>(((g.b_resident ? ka : s) * sb_stride) >> 4);
+                        const uint64_t db = bdesc0 + static_cast<uint64_t>(g.b_resident ? ka : s) * b_chunk_step;
 #pragma unroll
                         for (int k = 0; k < CB / 32; ++k)
                             mma_i8(d, da0 + 2 * k, db + 2 * k, idesc, (ka | k) != 0 ? 1u : 0u);
@@ -625,25 +649,30 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             if (!mbar_wait(donebar, 0)) atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
         }
     } else {
-        // ---------------- epilogue: TMEM lanes 32*(warp%4) .. +31 = tile rows;
-        // the kEpiWarps/4 warps of a quadrant take interleaved 16-column groups
+        // ---------------- epilogue: TMEM lanes 32*(warp%4) .. +31 = tile rows.
+        // Warps form NA groups; group gi drains accumulator gi, i.e. tiles t = gi (mod NA),
+        // so NA tiles are in flight.  Inside a group the warps of a quadrant take
+        // interleaved 16-column groups.
+        const int ew = warp - 2;
+        const int gi = ew / group_warps;
         const int quad = warp & 3;
-        const int slice = (warp - 2) >> 2;
-        constexpr int kSlices = kEpiWarps / 4;
+        const int slice = (ew % group_warps) >> 2;
+        const int kSlices = group_warps / 4;
         const int r = quad * 32 + lane;
         const int tw = g.TW, th = g.TH;
         const int rn = r / (tw * th), rh = (r / tw) % th, rw = r % tw;
         const bool in_tile = r < tw * th * g.TN;
         const int tile_end = min(e.cout, (nt + 1) * BN);
-        const int ncg = bn32 / 16;
-        int t = 0;
-        for (int mt = blockIdx.x; mt < g.m_tiles; mt += gridDim.x, ++t) {
-            const int buf = t & 1;
-            const uint32_t use = static_cast<uint32_t>(t >> 1);
+        const int ncg = bn32 / 32;   // 32-column groups, each handled as two 16-column halves
+        constexpr int n_out = NOUT;
+        int t = gi;
+        for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NA * gridDim.x, t += NA) {
+            const int buf = gi;
+            const uint32_t use = static_cast<uint32_t>(t / NA);
             int n, h, w;
             bool valid;
             size_t pq;
-            if (g.mode == 1) {
+            if (MODE == 1) {
                 const size_t q = static_cast<size_t>(mt) * 128 + r;
                 const size_t img = static_cast<size_t>(g.Hp) * g.Wp;
                 n = static_cast<int>(q / img);
@@ -662,42 +691,64 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 pq = (static_cast<size_t>(n) * (g.OH + 2) + h + 1) * (g.OW + 2) + w + 1;
             }
             const size_t pf = (static_cast<size_t>(n) * g.OH + h) * g.OW + w;
-            // the residual does not depend on the MMAs: fetch the first group before waiting
+            // the residual does not depend on the MMAs: fetch the first half before waiting
             float res[16];
             {
-                const int c0 = nt * BN + slice * 16;
-                if (e.post != 0 && valid && slice < ncg && c0 < tile_end) load_res16(e, pf, c0, min(16, tile_end - c0), res);
+                const int c0 = nt * BN + slice * 32;
+                if (RES && valid && slice < ncg && c0 < tile_end) load_res16(e, pf, c0, min(16, tile_end - c0), res);
             }
             if (!mbar_wait(accf0 + 8 * buf, use & 1u)) {
                 atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
                 break;
             }
             tc_fence_after();
+            const uint32_t trow = tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16);
             for (int cg = slice; cg < ncg; cg += kSlices) {
-                uint32_t v[16];
-                __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the per-lane stores
-                tmem_ld16(tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16) +
-                              cg * 16,
-                          v);
-                tmem_wait_ld();
-                const int c0 = nt * BN + cg * 16;
-                if (!valid || c0 >= tile_end) continue;
-                const int nv = min(16, tile_end - c0);
-                float y[16];
-                const float4* f4 = reinterpret_cast<const float4*>(s_factor + cg * 16);
-                const float4* b4 = reinterpret_cast<const float4*>(s_bias + cg * 16);
+                const int c0 = nt * BN + cg * 32;
+                const int nv32 = min(32, tile_end - c0);   // valid channels of this 32-group (may be <= 0)
+                uint32_t wq[2][8];                          // codes of both halves, per output
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float4 f = f4[j], bb = b4[j];
-                    y[4 * j + 0] = apply_act(__fadd_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[4 * j + 0])), f.x), bb.x), e.act);
-                    y[4 * j + 1] = apply_act(__fadd_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[4 * j + 1])), f.y), bb.y), e.act);
-                    y[4 * j + 2] = apply_act(__fadd_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[4 * j + 2])), f.z), bb.z), e.act);
-                    y[4 * j + 3] = apply_act(__fadd_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[4 * j + 3])), f.w), bb.w), e.act);
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t v[16];
+                    __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the per-lane stores
+                    tmem_ld16(trow + cg * 32 + hh * 16, v);
+                    tmem_wait_ld();
+                    const int ch = c0 + hh * 16;
+                    const int nv = min(16, tile_end - ch);
+                    if (!valid || nv <= 0) continue;
+                    float y[16];
+                    dequant16(v, s_factor + cg * 32 + hh * 16, s_bias + cg * 32 + hh * 16, e.act, y);
+                    finish16<RES, F32>(e, pf, ch, nv, y, res);
+                    // prefetch the next residual half of this warp
+                    {
+                        const int cn = hh == 0 ? ch + 16 : c0 + 32 * kSlices;
+                        if (RES && (hh == 0 || cg + kSlices < ncg) && cn < tile_end)
+                            load_res16(e, pf, cn, min(16, tile_end - cn), res);
+                    }
+#pragma unroll
+                    for (int o = 0; o < 2; ++o) {
+                        if (o >= n_out) continue;
+                        const float inv = o == 0 ? e.inv0 : e.inv1;
+                        const double s = o == 0 ? e.s0 : e.s1;
+                        if (nv32 == 32) {
+                            uint32_t w4[4];
+                            quant16(y, inv, s, w4);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) wq[o][hh * 4 + j] = w4[j];
+                        } else {
+                            int8_t* qp = code_ptr(e, o, pq, n, ch);
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (j < nv) qp[j] = sat8(quant_code(y[j], inv, s));
+                        }
+                    }
                 }
-                epilogue_store16(e, pf, pq, n, c0, nv, y, res);
-                // prefetch the residual of this warp's next column group
-                const int cn = c0 + 16 * kSlices;
-                if (e.post != 0 && cg + kSlices < ncg && cn < tile_end) load_res16(e, pf, cn, min(16, tile_end - cn), res);
+                // full 32-channel groups: one 32-byte (full-sector) store per output
+                if (valid && nv32 == 32) {
+#pragma unroll
+                    for (int o = 0; o < 2; ++o)
+                        if (o < n_out) st_v8(reinterpret_cast<uint32_t*>(code_ptr(e, o, pq, n, c0)), wq[o]);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -706,7 +757,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, 2 * g.acc_cols);
+    if (warp == 1) tmem_dealloc(tmem, NA * g.acc_cols);
 }
 
 // ------------------------------------------------------------------ stem im2col
