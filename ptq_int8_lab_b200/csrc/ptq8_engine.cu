@@ -270,6 +270,7 @@ bool decompose(ConvQ& cq, int H, int W, std::string* note) {
     cq.bias.swap(nb);
     cq.view_oh = OH;
     cq.view_ow = OW;
+    c.cout = ncout;
     c.kh = th;
     c.kw = tw;
     c.sh = c.sw = 1;
