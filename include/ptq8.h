@@ -77,6 +77,27 @@ int ptq8_quantize_weight(const float* w, int cout, int k, int bits, int8_t* code
  * with s = ptq8_act_scale(lo, hi, 8, mode) (ref_int8.py:89-91).  Test entry point. */
 int ptq8_quantize_device(int device, const float* x_host, size_t n, float lo, float hi, int mode, int8_t* codes);
 
+/* Same codes as ptq8_quantize_device, but the call allocates no device memory
+ * (no cudaMalloc / cudaFree, no allocating library routine).  No counterpart in
+ * the reference.  For callers that cannot allocate: a process whose free device
+ * memory is held by another allocator (a framework's caching pool, a serving
+ * process at its memory cap) where a cudaMalloc may fail, and code that cannot
+ * take the device-wide synchronisation cudaFree implies while other streams run.
+ *
+ * The input and output stay the caller's host buffers.  The device staging for
+ * them is a fixed array inside the library, one per device, holding at most
+ * PTQ8_NOALLOC_MAX_VALUES values (4 MiB of floats + 1 MiB of codes); a larger n
+ * is rejected with PTQ8_ERR_INVALID and a message in err.  The first call on a
+ * device looks that array up (with the device current) and so does set-up work:
+ * make it before any stream capture.  All calls on a device share the array and
+ * leave their data in it, so calls that overlap in time (two host threads on the
+ * same device) race and must be serialised by the caller.  Copies and the kernel
+ * run on the legacy default stream; the call returns when the codes are on the
+ * host.  err (may be NULL) receives "" on success. */
+#define PTQ8_NOALLOC_MAX_VALUES (1u << 20)
+int ptq8_quantize_device_noalloc(int device, const float* x_host, size_t n, float lo, float hi, int mode,
+                                 int8_t* codes, char* err, size_t errlen);
+
 /* ---- engine ---------------------------------------------------------------- */
 
 /* Int8Engine construction on CUDA device `device` (int8_engine.cuh:130). */

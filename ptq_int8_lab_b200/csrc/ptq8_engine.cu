@@ -19,6 +19,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -880,6 +881,39 @@ void copy_err(const std::string& m, char* err, size_t errlen) {
 
 }  // namespace
 
+// ---------------------------------------------------------------- fixed scratch
+// Device memory of ptq8_quantize_device_noalloc, part of the loaded module (one
+// copy per device), so the call never allocates: PTQ8_NOALLOC_MAX_VALUES float
+// inputs, then as many code bytes.  Every call on a device reuses the same bytes
+// and leaves its own data behind; nothing here has to start at zero because the
+// call reads back only the codes its kernel has just written.
+constexpr size_t kNoAllocCodesOff = static_cast<size_t>(PTQ8_NOALLOC_MAX_VALUES) * 4;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocCodesOff + PTQ8_NOALLOC_MAX_VALUES];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Address of g_noalloc_scratch on `device` (which must be current), looked up on
+// the first call for that device and remembered.
+unsigned char* noalloc_scratch(int device, std::string& why) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void* p = nullptr;
+        const cudaError_t ce = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (ce != cudaSuccess || !p) {
+            why = strf("cudaGetSymbolAddress of the fixed scratch failed: %s", cudaGetErrorString(ce));
+            return nullptr;
+        }
+        g_noalloc_ptr[device] = static_cast<unsigned char*>(p);
+    }
+    return g_noalloc_ptr[device];
+}
+
+}  // namespace
+
 // ====================================================================== C ABI
 
 extern "C" {
@@ -1019,6 +1053,56 @@ int ptq8_quantize_device(int device, const float* x_host, size_t n, float lo, fl
     cudaFree(dx);
     cudaFree(dq);
     return rc;
+}
+
+int ptq8_quantize_device_noalloc(int device, const float* x_host, size_t n, float lo, float hi, int mode,
+                                 int8_t* codes, char* err, size_t errlen) {
+    if (!x_host || !codes) {
+        copy_err("null input or output pointer", err, errlen);
+        return PTQ8_ERR_INVALID;
+    }
+    if (device < 0 || device >= kNoAllocMaxDevices) {
+        copy_err(strf("device %d out of range [0, %d)", device, kNoAllocMaxDevices), err, errlen);
+        return PTQ8_ERR_INVALID;
+    }
+    if (n > static_cast<size_t>(PTQ8_NOALLOC_MAX_VALUES)) {
+        copy_err(strf("n = %zu exceeds the fixed scratch of %u values; split the call or use ptq8_quantize_device",
+                      n, static_cast<unsigned>(PTQ8_NOALLOC_MAX_VALUES)),
+                 err, errlen);
+        return PTQ8_ERR_INVALID;
+    }
+    cudaError_t ce = cudaSetDevice(device);
+    if (ce != cudaSuccess) {
+        copy_err(strf("cudaSetDevice(%d): %s", device, cudaGetErrorString(ce)), err, errlen);
+        return PTQ8_ERR_CUDA;
+    }
+    std::string why;
+    unsigned char* base = noalloc_scratch(device, why);
+    if (!base) {
+        copy_err(why, err, errlen);
+        return PTQ8_ERR_CUDA;
+    }
+    if (n == 0) {
+        copy_err("", err, errlen);
+        return PTQ8_OK;
+    }
+    float* dx = reinterpret_cast<float*>(base);
+    int8_t* dq = reinterpret_cast<int8_t*>(base + kNoAllocCodesOff);
+    const double s = act_scale_from_range(lo, hi, 8, mode);
+    // Legacy default stream throughout: the device-to-host copy is ordered after the kernel.
+    ce = cudaMemcpy(dx, x_host, n * 4, cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) {
+        const size_t groups = (n + 31) / 32;
+        quantize_kernel<<<(unsigned)((groups + 127) / 128), 128>>>(dx, n, (float)(1.0 / s), s, dq);
+        ce = cudaGetLastError();
+    }
+    if (ce == cudaSuccess) ce = cudaMemcpy(codes, dq, n, cudaMemcpyDeviceToHost);
+    if (ce != cudaSuccess) {
+        copy_err(strf("CUDA: %s", cudaGetErrorString(ce)), err, errlen);
+        return PTQ8_ERR_CUDA;
+    }
+    copy_err("", err, errlen);
+    return PTQ8_OK;
 }
 
 ptq8_engine* ptq8_engine_create(int device) {

@@ -37,6 +37,7 @@ ACT_MINMAX = 1
 EXPORTS = (
     "ptq8_abi_version", "ptq8_model_load", "ptq8_model_free", "ptq8_model_info", "ptq8_model_conv",
     "ptq8_model_block", "ptq8_model_weights", "ptq8_load_ptqc", "ptq8_act_scale", "ptq8_quantize_weight", "ptq8_quantize_device",
+    "ptq8_quantize_device_noalloc",
     "ptq8_engine_create", "ptq8_engine_destroy", "ptq8_engine_last_error", "ptq8_engine_build",
     "ptq8_engine_set_act_mode", "ptq8_engine_set_calib", "ptq8_engine_set_input_shape",
     "ptq8_engine_alloc_scratch", "ptq8_engine_set_stream", "ptq8_engine_stream", "ptq8_engine_forward",
@@ -75,6 +76,8 @@ def lib() -> ctypes.CDLL:
         "ptq8_quantize_weight": (c_int, [P(ctypes.c_float), c_int, c_int, c_int, P(ctypes.c_int8), P(ctypes.c_float)]),
         "ptq8_quantize_device": (c_int, [c_int, P(ctypes.c_float), c_size, ctypes.c_float, ctypes.c_float, c_int,
                                          P(ctypes.c_int8)]),
+        "ptq8_quantize_device_noalloc": (c_int, [c_int, P(ctypes.c_float), c_size, ctypes.c_float, ctypes.c_float,
+                                                 c_int, P(ctypes.c_int8), c_char_p, c_size]),
         "ptq8_engine_create": (c_void_p, [c_int]),
         "ptq8_engine_destroy": (None, [c_void_p]),
         "ptq8_engine_last_error": (c_char_p, [c_void_p]),
