@@ -728,8 +728,16 @@ EpiParams epi_for(ptq8_engine* e, const Step& st) {
     p.out_q0 = out.codes.size() > 0 ? out.codes[0] : nullptr;
     p.out_q1 = out.codes.size() > 1 ? out.codes[1] : nullptr;
     p.ldq0 = p.ldq1 = out.ldq;
-    if (out.scales.size() > 0) { p.s0 = out.scales[0]; p.inv0 = (float)(1.0 / out.scales[0]); }
-    if (out.scales.size() > 1) { p.s1 = out.scales[1]; p.inv1 = (float)(1.0 / out.scales[1]); }
+    if (out.scales.size() > 0) {
+        p.s0 = out.scales[0];
+        p.inv0 = (float)(1.0 / out.scales[0]);
+        p.q0 = make_qparams(out.scales[0]);
+    }
+    if (out.scales.size() > 1) {
+        p.s1 = out.scales[1];
+        p.inv1 = (float)(1.0 / out.scales[1]);
+        p.q1 = make_qparams(out.scales[1]);
+    }
     return p;
 }
 
@@ -1045,8 +1053,8 @@ int ptq8_quantize_device(int device, const float* x_host, size_t n, float lo, fl
     int rc = PTQ8_OK;
     if (cudaMemcpy(dx, x_host, n * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = PTQ8_ERR_CUDA;
     if (!rc && n) {
-        const size_t groups = (n + 31) / 32;
-        quantize_kernel<<<(unsigned)((groups + 127) / 128), 128>>>(dx, n, (float)(1.0 / s), s, dq);
+        const size_t groups = (n + 15) / 16;
+        quantize_kernel<<<(unsigned)((groups + 127) / 128), 128>>>(dx, n, make_qparams(s), (float)(1.0 / s), s, dq);
         if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) rc = PTQ8_ERR_CUDA;
     }
     if (!rc && cudaMemcpy(codes, dq, n, cudaMemcpyDeviceToHost) != cudaSuccess) rc = PTQ8_ERR_CUDA;
@@ -1092,8 +1100,8 @@ int ptq8_quantize_device_noalloc(int device, const float* x_host, size_t n, floa
     // Legacy default stream throughout: the device-to-host copy is ordered after the kernel.
     ce = cudaMemcpy(dx, x_host, n * 4, cudaMemcpyHostToDevice);
     if (ce == cudaSuccess) {
-        const size_t groups = (n + 31) / 32;
-        quantize_kernel<<<(unsigned)((groups + 127) / 128), 128>>>(dx, n, (float)(1.0 / s), s, dq);
+        const size_t groups = (n + 15) / 16;
+        quantize_kernel<<<(unsigned)((groups + 127) / 128), 128>>>(dx, n, make_qparams(s), (float)(1.0 / s), s, dq);
         ce = cudaGetLastError();
     }
     if (ce == cudaSuccess) ce = cudaMemcpy(codes, dq, n, cudaMemcpyDeviceToHost);

@@ -23,6 +23,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cmath>
+
 namespace ptq8 {
 
 // Sticky device error word: a bounded wait that ran out records where.
@@ -243,48 +245,85 @@ __device__ __forceinline__ int quant_exact(float y, double s) {
     return static_cast<int>(q);
 }
 
-// Rare path: 32 codes with the exact formula (kept out of line: small hot loop).
-__device__ __noinline__ void quant32_exact(const float* y, double s, uint32_t* w) {
-    for (int j = 0; j < 8; ++j)
-        w[j] = pack4(quant_exact(y[4 * j], s), quant_exact(y[4 * j + 1], s), quant_exact(y[4 * j + 2], s),
-                     quant_exact(y[4 * j + 3], s));
+// Two-lane float add with one IEEE rounding per lane (add.rn.f32x2).
+//
+// The dequantization's multiply and add stay scalar (__fmul_rn, __fadd_rn):
+// written as mul.rn.f32x2 followed by add.rn.f32x2, on sm_100a with CUDA 12.9,
+// the pair gave results one ulp away from two separate roundings, as a fused
+// multiply-add would.
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 r;
+    asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\t"
+        "mov.b64 pb, {%4, %5};\n\t"
+        "add.rn.f32x2 pd, pa, pb;\n\t"
+        "mov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
 }
 
-// 32 int8 codes of y (scale s, inv = float(1/s)) packed into 8 words.
-__device__ __forceinline__ void quant32(const float (&y)[32], float inv, double s, uint32_t (&w)[8]) {
-    uint32_t flag = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int a = quant_fast(y[4 * j], inv, flag), b = quant_fast(y[4 * j + 1], inv, flag);
-        const int c = quant_fast(y[4 * j + 2], inv, flag), d = quant_fast(y[4 * j + 3], inv, flag);
-        w[j] = pack4(a, b, c, d);
-    }
-    if (flag) {
-        float ys[32];
-        uint32_t ws[8];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) ys[j] = y[j];
-        quant32_exact(ys, s, ws);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = ws[j];
-    }
+// Multipliers that bracket 1/s, inv_lo < 1/s < inv_hi (relative gaps near
+// 2^-22), and the float32 values y_lo ~ -128 s, y_hi ~ 127 s past which codes
+// saturate.  y_hi / s and y_lo / s are within 2^-24 relative of 127 and -128, so
+// clamping y to [y_lo, y_hi] never changes a code.
+struct QParams {
+    float inv_lo, inv_hi, y_lo, y_hi;
+};
+
+inline QParams make_qparams(double s) {
+    const double inv = 1.0 / s;
+    float lo = static_cast<float>(inv * (1.0 - 0x1p-22));
+    float hi = static_cast<float>(inv * (1.0 + 0x1p-22));
+    while (static_cast<double>(lo) >= inv * (1.0 - 0x1p-23)) lo = std::nextafter(lo, 0.0f);
+    while (static_cast<double>(hi) <= inv * (1.0 + 0x1p-23)) hi = std::nextafter(hi, HUGE_VALF);
+    return {lo, hi, static_cast<float>(-128.0 * s), static_cast<float>(127.0 * s)};
 }
 
+// Rare path: 16 codes with the exact formula (kept out of line: small hot loop).
 __device__ __noinline__ void quant16_exact(const float* y, double s, uint32_t* w) {
     for (int j = 0; j < 4; ++j)
         w[j] = pack4(quant_exact(y[4 * j], s), quant_exact(y[4 * j + 1], s), quant_exact(y[4 * j + 2], s),
                      quant_exact(y[4 * j + 3], s));
 }
 
-// 16 int8 codes of y packed into 4 words.
-__device__ __forceinline__ void quant16(const float (&y)[16], float inv, double s, uint32_t (&w)[4]) {
-    uint32_t flag = 0;
+// 16 codes clip(round_half_away(double(y[j]) / s), -128, 127) packed into 4 words
+// (byte b of word k = code 4k+b).
+//
+// Each clamped y is multiplied by both bracketing multipliers with 1.5*2^23
+// added in the same FMA.  |y * inv| < 2^8, so the exact sum lies in
+// [2^23, 2^24) where the float spacing is 1: the FMA returns 1.5*2^23 +
+// RNE(y * inv), and the code is the low byte of its bits.  When the two results
+// agree on an integer k, the closed interval [y*inv_lo, y*inv_hi] sits inside
+// [k-1/2, k+1/2]; double(y)/s lies strictly inside that interval with a gap far
+// larger than its float64 rounding, so it rounds (half away) to k as well.
+// Otherwise a half-integer lies in between and the float64 formula decides for
+// the 16 values.  `lower`: y may lie below y_lo (false when y >= 0 is known).
+__device__ __forceinline__ void quant16q(const float (&y)[16], const QParams& q, double s, bool lower,
+                                         uint32_t (&w)[4]) {
+    const float2 lo2 = make_float2(q.inv_lo, q.inv_lo);
+    const float2 hi2 = make_float2(q.inv_hi, q.inv_hi);
+    const float2 mg = make_float2(kRoundMagic, kRoundMagic);
+    uint32_t flag = 0, m[16];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int a = quant_fast(y[4 * j], inv, flag), b = quant_fast(y[4 * j + 1], inv, flag);
-        const int c = quant_fast(y[4 * j + 2], inv, flag), d = quant_fast(y[4 * j + 3], inv, flag);
-        w[j] = pack4(a, b, c, d);
+    for (int j = 0; j < 16; j += 2) {
+        float c0 = fminf(y[j], q.y_hi), c1 = fminf(y[j + 1], q.y_hi);
+        if (lower) {
+            c0 = fmaxf(c0, q.y_lo);
+            c1 = fmaxf(c1, q.y_lo);
+        }
+        const float2 c = make_float2(c0, c1);
+        const float2 a = __ffma2_rn(c, lo2, mg);
+        const float2 b = __ffma2_rn(c, hi2, mg);
+        flag |= __float_as_uint(a.x) ^ __float_as_uint(b.x);
+        flag |= __float_as_uint(a.y) ^ __float_as_uint(b.y);
+        m[j] = __float_as_uint(a.x);
+        m[j + 1] = __float_as_uint(a.y);
     }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        w[k] = __byte_perm(__byte_perm(m[4 * k], m[4 * k + 1], 0x0040), __byte_perm(m[4 * k + 2], m[4 * k + 3], 0x0040),
+                           0x5410);
     if (flag) {
         float ys[16];
         uint32_t ws[4];
@@ -339,6 +378,7 @@ struct EpiParams {
     int ldq0, ldq1;
     float inv0, inv1;
     double s0, s1;
+    QParams q0, q1;         // bracketing multipliers / saturation bounds of s0, s1
     int cout;
     int vec32;  // 1 when fp32 rows are 32-byte aligned (cout % 8 == 0): 256-bit loads/stores allowed
     int act;    // activation of the conv itself: 0 none / 1 relu / 2 relu6
@@ -362,12 +402,29 @@ __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0
 
 // Dequantize 16 accumulators of channels [c, c+16) (factor/bias from shared
 // memory): y = act(fadd(fmul(float(acc), factor), bias)), two roundings.
+//
+// float(acc): acc + 0x4B400000 is the bit pattern of 1.5*2^23 + acc when
+// |acc| < 2^22 (exact subtraction afterwards); in that range the pattern xor
+// 0x4B000000 stays below 2^23, so one OR over the 16 patterns tells whether
+// every accumulator was in range.  Otherwise the rounding conversion is used.
 __device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float* sf, const float* sb, int act,
                                           float (&y)[16]) {
-    uint32_t big = 0;
+    uint32_t range = 0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = acc_to_float(v[j], big);
-    if (big) {   // |acc| >= 2^22 somewhere: convert with the rounding instruction
+    for (int j = 0; j < 16; ++j) {
+        const uint32_t bits = v[j] + static_cast<uint32_t>(kRoundMagicBits);
+        range |= bits ^ 0x4B000000u;
+        y[j] = __uint_as_float(bits);
+    }
+    if (range < 0x800000u) {
+        const float2 mg = make_float2(-kRoundMagic, -kRoundMagic);
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            const float2 t = add2_rn(make_float2(y[j], y[j + 1]), mg);
+            y[j] = t.x;
+            y[j + 1] = t.y;
+        }
+    } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] = __int2float_rn(static_cast<int>(v[j]));
     }
@@ -376,10 +433,17 @@ __device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float* 
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const float4 f = f4[j], bb = b4[j];
-        y[4 * j + 0] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 0], f.x), bb.x), act);
-        y[4 * j + 1] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 1], f.y), bb.y), act);
-        y[4 * j + 2] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 2], f.z), bb.z), act);
-        y[4 * j + 3] = apply_act(__fadd_rn(__fmul_rn(y[4 * j + 3], f.w), bb.w), act);
+        y[4 * j] = __fadd_rn(__fmul_rn(y[4 * j], f.x), bb.x);
+        y[4 * j + 1] = __fadd_rn(__fmul_rn(y[4 * j + 1], f.y), bb.y);
+        y[4 * j + 2] = __fadd_rn(__fmul_rn(y[4 * j + 2], f.z), bb.z);
+        y[4 * j + 3] = __fadd_rn(__fmul_rn(y[4 * j + 3], f.w), bb.w);
+    }
+    if (act == 1) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.0f);
+    } else if (act == 2) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = fminf(fmaxf(y[j], 0.0f), 6.0f);
     }
 }
 
@@ -389,7 +453,11 @@ __device__ __forceinline__ void finish16(const EpiParams& e, size_t pf, int c0, 
                                          const float (&r)[16]) {
     if constexpr (RES) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) y[j] = __fadd_rn(y[j], r[j]);
+        for (int j = 0; j < 16; j += 2) {
+            const float2 t = add2_rn(make_float2(y[j], y[j + 1]), make_float2(r[j], r[j + 1]));
+            y[j] = t.x;
+            y[j + 1] = t.y;
+        }
         if (e.post == 1) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.0f);
@@ -665,6 +733,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const int tile_end = min(e.cout, (nt + 1) * BN);
         const int ncg = bn32 / 32;   // 32-column groups, each handled as two 16-column halves
         constexpr int n_out = NOUT;
+        // codes can only saturate low when the values are not already clipped at zero
+        const bool lower = RES ? e.post != 1 : e.act == 0;
         int t = gi;
         for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NA * gridDim.x, t += NA) {
             const int buf = gi;
@@ -732,7 +802,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         const double s = o == 0 ? e.s0 : e.s1;
                         if (nv32 == 32) {
                             uint32_t w4[4];
-                            quant16(y, inv, s, w4);
+                            quant16q(y, o == 0 ? e.q0 : e.q1, s, lower, w4);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) wq[o][hh * 4 + j] = w4[j];
                         } else {
@@ -903,20 +973,21 @@ __global__ void maxpool_kernel(const float* __restrict__ in, int N, int H, int W
 
 // ------------------------------------------------------------------ quantize (test entry)
 
-// codes[i] of x[i] through the same device paths the epilogues use: quant32 on
-// full groups of 32, quant_code on the tail.
-__global__ void quantize_kernel(const float* __restrict__ x, size_t n, float inv, double s, int8_t* __restrict__ out) {
+// codes[i] of x[i] through the same device paths the epilogues use: quant16q
+// on full groups of 16, quant_code on the tail.
+__global__ void quantize_kernel(const float* __restrict__ x, size_t n, QParams q, float inv, double s,
+                                int8_t* __restrict__ out) {
     const size_t g = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
-    const size_t base = g * 32;
+    const size_t base = g * 16;
     if (base >= n) return;
-    if (base + 32 <= n) {
-        float y[32];
+    if (base + 16 <= n) {
+        float y[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = x[base + j];
-        uint32_t w[8];
-        quant32(y, inv, s, w);
+        for (int j = 0; j < 16; ++j) y[j] = x[base + j];
+        uint32_t w[4];
+        quant16q(y, q, s, true, w);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) reinterpret_cast<uint32_t*>(out + base)[j] = w[j];
+        for (int j = 0; j < 4; ++j) reinterpret_cast<uint32_t*>(out + base)[j] = w[j];
     } else {
         for (size_t i = base; i < n; ++i) out[i] = sat8(quant_code(x[i], inv, s));
     }
