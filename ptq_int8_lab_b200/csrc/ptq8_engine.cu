@@ -770,9 +770,13 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     }
     if (st.kind == K_STEM_IM2COL) {
         const ConvSpec& c = e->q[st.conv].spec;
-        const int rows = std::max(1, std::min(st.oh, 4096 / std::max(1, st.ow * st.kpad / 4)));
+        // whole images per CTA while the quantized band stays within 24 KB of shared memory
+        const size_t band_w = (size_t)(st.ow - 1) * c.sw + c.kw;
+        int rows = st.oh;
+        while (rows > 1 && (size_t)c.cin * ((rows - 1) * c.sh + c.kh) * band_w > 24 * 1024) rows = (rows + 1) / 2;
         const int bands = (st.oh + rows - 1) / rows;
-        const size_t band_bytes = (size_t)c.cin * ((rows - 1) * c.sh + c.kh) * ((st.ow - 1) * c.sw + c.kw);
+        const size_t band_bytes =
+            (((size_t)c.cin * ((rows - 1) * c.sh + c.kh) * band_w + 15) & ~(size_t)15) + (size_t)st.kpad * sizeof(int);
         stem_im2col_kernel<<<n * bands, 256, band_bytes, s>>>(e->d_input, st.d_im2col, n, c.cin, st.ih, st.iw, st.oh,
                                                               st.ow, c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad,
                                                               rows, (float)(1.0 / st.s_in), st.s_in);

@@ -834,51 +834,69 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 
 // x: fp32 NCHW [N][C][H][W]; out: int8 [N*OH*OW][kpad] with k = (i*KW + j)*C + c,
 // codes of the stem's scale, zero for out-of-image taps and k >= KH*KW*C.
-// One CTA per band of `rows` output rows of one image: the input band is read
-// once (coalesced), quantized once into shared memory (with zero padding),
-// then the im2col rows are written as consecutive 32-bit words.
+// One CTA per band of `rows` output rows of one image.  The input band is read
+// once (one warp per band row, coalesced) and quantized once into shared
+// memory with its zero padding; a table maps k to its offset in the band; then
+// each thread assembles the kpad-byte im2col row of one output pixel and writes
+// it with 16-byte stores (consecutive pixels: consecutive rows).
 __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restrict__ out, int N, int C, int H,
                                    int W, int OH, int OW, int KH, int KW, int SH, int SW, int PH, int PW,
                                    int kpad, int rows, float inv, double s) {
-    extern __shared__ int8_t band[];   // [C][band_h][band_w]
+    extern __shared__ __align__(16) int8_t band[];   // [C][band_h][band_w], then int koff[kpad]
     const int bands = (OH + rows - 1) / rows;
     const int n = blockIdx.x / bands;
-    const int r0 = (blockIdx.x % bands) * rows;
+    const int r0 = (blockIdx.x - n * bands) * rows;
     const int r1 = min(OH, r0 + rows);
     const int band_h = (rows - 1) * SH + KH;
     const int band_w = (OW - 1) * SW + KW;
+    const int band_bytes = C * band_h * band_w;
+    int* koff = reinterpret_cast<int*>(band + ((band_bytes + 15) & ~15));
+    const int K = KH * KW * C;
+    for (int k = threadIdx.x; k < kpad; k += blockDim.x) {
+        int o = -1;
+        if (k < K) {
+            const int c = k % C, tap = k / C;
+            o = (c * band_h + tap / KW) * band_w + tap % KW;
+        }
+        koff[k] = o;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const int ih0 = r0 * SH - PH, iw0 = -PW;
-    for (int idx = threadIdx.x; idx < C * band_h * band_w; idx += blockDim.x) {
-        const int bw = idx % band_w;
-        const int bh = (idx / band_w) % band_h;
-        const int c = idx / (band_w * band_h);
-        const int ih = ih0 + bh, iw = iw0 + bw;
-        int q = 0;
-        if (ih >= 0 && ih < H && iw >= 0 && iw < W)
-            q = sat8(quant_code(__ldg(x + ((static_cast<size_t>(n) * C + c) * H + ih) * W + iw), inv, s));
-        band[idx] = static_cast<int8_t>(q);
+    for (int rr = warp; rr < C * band_h; rr += nwarps) {
+        const int c = rr / band_h, bh = rr - (rr / band_h) * band_h;
+        const int ih = ih0 + bh;
+        const bool row_in = ih >= 0 && ih < H;
+        const float* xr = x + ((static_cast<size_t>(n) * C + c) * H + (row_in ? ih : 0)) * W;
+        int8_t* br = band + rr * band_w;
+        for (int bw = lane; bw < band_w; bw += 32) {
+            const int iw = iw0 + bw;
+            int q = 0;
+            if (row_in && iw >= 0 && iw < W) q = sat8(quant_code(__ldg(xr + iw), inv, s));
+            br[bw] = static_cast<int8_t>(q);
+        }
     }
     __syncthreads();
-    const int words = kpad / 4;
-    const int K = KH * KW * C;
-    const int total = (r1 - r0) * OW * words;
-    uint32_t* orow = reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(n) * OH + r0) * OW * kpad);
-    for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
-        const int wd = idx % words;
-        const int pos = idx / words;
-        const int ow = pos % OW, ohl = pos / OW;
-        uint32_t packed = 0;
+    const int npix = (r1 - r0) * OW;
+    int8_t* obase = out + (static_cast<size_t>(n) * OH + r0) * OW * kpad;
+    for (int p = threadIdx.x; p < npix; p += blockDim.x) {
+        const int ohl = p / OW, ow = p - (p / OW) * OW;
+        const int8_t* bp = band + ohl * SH * band_w + ow * SW;
+        uint4* op = reinterpret_cast<uint4*>(obase + static_cast<size_t>(p) * kpad);
+        for (int k0 = 0; k0 < kpad; k0 += 16) {
+            uint32_t wv[4];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int k = wd * 4 + b;
-            if (k < K) {
-                const int c = k % C, tap = k / C;
-                const int i = tap / KW, j = tap - (tap / KW) * KW;
-                const uint32_t q = static_cast<uint8_t>(band[(c * band_h + ohl * SH + i) * band_w + ow * SW + j]);
-                packed |= q << (8 * b);
+            for (int wd = 0; wd < 4; ++wd) {
+                uint32_t packed = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int o = koff[k0 + wd * 4 + b];
+                    const uint32_t q = o >= 0 ? static_cast<uint8_t>(bp[o]) : 0u;
+                    packed |= q << (8 * b);
+                }
+                wv[wd] = packed;
             }
+            op[k0 >> 4] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
-        orow[idx] = packed;
     }
 }
 
