@@ -24,6 +24,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from datetime import datetime
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -35,7 +36,7 @@ METRIC = "int8 images/sec ResNet-18 W8A8 32x32 at 1/2/4/8 B200; % of int8 TC/HBM
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=8192, help="images per GPU")
@@ -65,8 +66,12 @@ def model_files(cache: str, rank: int, world: int, barrier):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks / throttle reasons, sampled every 100 ms.
+
+    Started before the warm-up (NVML start-up takes a while); each sample carries
+    a host timestamp, and only samples inside [t0, t1] of the timed region are
+    summarised (the nearest sample on each side when none falls inside)."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -75,15 +80,28 @@ class ClockSampler:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.p = None
 
-    def start(self):
+    def start(self, wait_s: float = 5.0):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+            return
+        t_end = time.time() + wait_s          # until the first sample has been written
+        while time.time() < t_end and self.p.poll() is None:
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.02)
 
-    def stop(self) -> dict:
+    @staticmethod
+    def _ts(field: str):
+        try:
+            return datetime.strptime(field.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
+
+    def stop(self, t0: float, t1: float) -> dict:
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
@@ -95,17 +113,22 @@ class ClockSampler:
         rows = []
         for line in open(self.f.name):
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
+            if len(parts) >= 10 and self._ts(parts[0]) is not None:
                 rows.append(parts)
         os.unlink(self.f.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "", 1).isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "", 1).isdigit()]
+        inside = [r for r in rows if t0 <= self._ts(r[0]) <= t1]
+        if not inside:
+            before = [r for r in rows if self._ts(r[0]) < t0][-1:]
+            after = [r for r in rows if self._ts(r[0]) > t1][:1]
+            inside = before + after
+        sm = [float(r[2]) for r in inside if r[2].replace(".", "", 1).isdigit()]
+        mx = [float(r[3]) for r in inside if r[3].replace(".", "", 1).isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        reasons = sorted({names[k] for r in inside for k in range(4) if r[6 + k].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(inside)}
 
 
 def measured_peaks():
@@ -221,22 +244,23 @@ def main():
             eng.copy_logits(B, logits.data_ptr())          # same stream as the collective
             dist.all_gather_into_tensor(gathered, logits)
 
+    clocks = ClockSampler(local)
+    clocks.start()
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
     eng.sync()
-    clocks = ClockSampler(local)
-    clocks.start()
     barrier()
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
     ev0.record(stream)
     for _ in range(a.steps):
         step()
     ev1.record(stream)
     torch.cuda.synchronize()
-    clk = clocks.stop()
+    clk = clocks.stop(t_wall0, time.time())
     ms = ev0.elapsed_time(ev1)
     eng.sync()
     if world > 1:

@@ -231,9 +231,10 @@ bool uniform_dim(int H, int k, int p, int s, int* OH, int* t, std::vector<int>* 
 // Positional decomposition (push_decompose.py:99-202): a conv whose input map is
 // no larger than its kernel becomes one th x tw conv with OH*OW*cout outputs
 // (position-major weight blocks, tiled bias) followed by DepthToSpace(DCR).
-// In NHWC memory the DCR rearrangement is the identity: output channel
-// (i*OW+j)*cout + c of image n is element (n, i, j, c).  Codes and scales are
-// sliced from the quantized kernel, so the accumulators are unchanged.
+// The epilogue applies the DCR rearrangement as it writes: output channel
+// (i*OW+j)*cout + c of image n goes to element (n, i, j, c) of the OH x OW map
+// (code_ptr for codes, f32_at for the fp32 map).  Codes and scales are sliced
+// from the quantized kernel, so the accumulators are unchanged.
 bool decompose(ConvQ& cq, int H, int W, std::string* note) {
     ConvSpec& c = cq.spec;
     if (c.groups != 1 || c.kh != c.kw || c.kh % 2 == 0) return false;
@@ -543,7 +544,9 @@ int finalize(ptq8_engine* e, int max_batch) {
         const size_t pix = NB * v.h * v.w;
         v.codes.assign(v.scales.size(), nullptr);
         if (vi == 0) continue;   // network input lives in d_input
-        if (v.need_f32 && !e->dalloc(&v.f32, pix * v.c * sizeof(float), "alloc fp32 activation")) return PTQ8_ERR_CUDA;
+        // fp32 maps use the f32_off layout: whole 32-position blocks
+        if (v.need_f32 && !e->dalloc(&v.f32, ((pix + 31) & ~(size_t)31) * v.c * sizeof(float), "alloc fp32 activation"))
+            return PTQ8_ERR_CUDA;
         // int8 codes carry a one-pixel zero border (written once, never touched again)
         const size_t bpix = NB * (v.h + 2) * (v.w + 2);
         for (size_t k = 0; k < v.scales.size(); ++k) {
@@ -1388,8 +1391,15 @@ int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst,
         }
         return PTQ8_OK;
     }
-    if (!e->cuda_ok(cudaMemcpy(host_dst, e->vals[e->final_val].f32, need, cudaMemcpyDeviceToHost), "dump"))
+    // the device map is in the f32_off layout: copy whole blocks, then reorder to NHWC
+    const Value& fv = e->vals[e->final_val];
+    const size_t npos = (size_t)n * shp[1] * shp[2];
+    std::vector<float> raw(((npos + 31) & ~(size_t)31) * fv.c);
+    if (!e->cuda_ok(cudaMemcpy(raw.data(), fv.f32, raw.size() * sizeof(float), cudaMemcpyDeviceToHost), "dump"))
         return PTQ8_ERR_CUDA;
+    float* dst = static_cast<float*>(host_dst);
+    for (size_t p = 0; p < npos; ++p)
+        for (int c = 0; c < fv.c; ++c) dst[p * fv.c + c] = raw[f32_off(p, c, fv.c)];
     return PTQ8_OK;
 }
 

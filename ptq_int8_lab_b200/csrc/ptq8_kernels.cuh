@@ -368,11 +368,24 @@ __device__ __forceinline__ float apply_act(float y, int act) {
 // Layouts: fp32 activations are NHWC [N][H][W][cout]; int8 code tensors are
 // NHWC with a one-pixel zero border, [N][H+2][W+2][ldq], so that stride-1
 // convs read every tap of a tile from one contiguous block (see conv_tc_kernel).
+// fp32 activation maps.  With C % 8 == 0 they are tiled as blocks of 32
+// positions x groups of 8 channels: element (p, c) at
+// ((p/32) * (C/8) + c/8) * 256 + (p%32) * 8 + c%8.  A thread's 8 channels stay
+// one 32-byte row, and the 32 lanes of a warp (consecutive positions) cover
+// 1 KB of consecutive bytes.  Other channel counts use plain NHWC [P][C].
+// Buffers hold a whole number of 32-position blocks.
+__host__ __device__ __forceinline__ size_t f32_off(size_t p, int c, int C) {
+    if ((C & 7) == 0)
+        return (((p >> 5) * static_cast<size_t>(C >> 3) + static_cast<size_t>(c >> 3)) << 8) + ((p & 31) << 3) +
+               static_cast<size_t>(c & 7);
+    return p * static_cast<size_t>(C) + c;
+}
+
 struct EpiParams {
     const float* factor;    // [cout] float(float(s_in) * w_scale[c])
     const float* bias;      // [cout]
-    const float* residual;  // fp32 NHWC [P][cout] or null
-    float* out_f32;         // fp32 NHWC [P][cout] or null
+    const float* residual;  // fp32 map [P][cout] (f32_off layout) or null
+    float* out_f32;         // fp32 map [P][cout] (f32_off layout) or null
     int8_t* out_q0;         // bordered int8 codes [N][OH+2][OW+2][ldq0] or null
     int8_t* out_q1;
     int ldq0, ldq1;
@@ -380,7 +393,7 @@ struct EpiParams {
     double s0, s1;
     QParams q0, q1;         // bracketing multipliers / saturation bounds of s0, s1
     int cout;
-    int vec32;  // 1 when fp32 rows are 32-byte aligned (cout % 8 == 0): 256-bit loads/stores allowed
+    int vec32;  // 1 when cout % 8 == 0: tiled fp32 maps, 256-bit loads/stores of 8 channels
     int act;    // activation of the conv itself: 0 none / 1 relu / 2 relu6
     int post;   // residual: 0 none, 1 add then relu, 2 add only
     // positional decomposition: channel c' = pos*dcr_oc + c of a 1x1 GEMM output is code
@@ -388,15 +401,31 @@ struct EpiParams {
     int dcr_oc, dcr_h, dcr_w;
 };
 
+// Element (pf, c) of the conv's output in its fp32 map: the position, channel
+// and channel count to pass to f32_off.  A positionally decomposed conv (one
+// output position per image, channel c = pos*dcr_oc + c') writes position pos
+// of its dcr_h x dcr_w map instead.  c must be the first of a group of 16.
+struct F32At {
+    size_t p;
+    int c, C;
+};
+__device__ __forceinline__ F32At f32_at(const EpiParams& e, size_t pf, int c) {
+    if (e.dcr_oc) {
+        const int pos = c / e.dcr_oc;
+        return {pf * static_cast<size_t>(e.dcr_h * e.dcr_w) + pos, c - pos * e.dcr_oc, e.dcr_oc};
+    }
+    return {pf, c, e.cout};
+}
+
 // Residual of 16 consecutive channels [c0, c0+16) of fp32 row pf (nv valid).
 __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0, int nv, float (&r)[16]) {
-    const float* rp = e.residual + pf * e.cout + c0;
+    const F32At a = f32_at(e, pf, c0);
     if (nv == 16 && e.vec32) {
-        ld_v8(rp, &r[0]);
-        ld_v8(rp + 8, &r[8]);
+        ld_v8(e.residual + f32_off(a.p, a.c, a.C), &r[0]);
+        ld_v8(e.residual + f32_off(a.p, a.c + 8, a.C), &r[8]);
     } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) r[j] = j < nv ? rp[j] : 0.0f;
+        for (int j = 0; j < 16; ++j) r[j] = j < nv ? e.residual[f32_off(a.p, a.c + j, a.C)] : 0.0f;
     }
 }
 
@@ -464,14 +493,14 @@ __device__ __forceinline__ void finish16(const EpiParams& e, size_t pf, int c0, 
         }
     }
     if constexpr (F32) {
-        float* op = e.out_f32 + pf * e.cout + c0;
+        const F32At a = f32_at(e, pf, c0);
         if (nv == 16 && e.vec32) {
-            st_v8(op, &y[0]);
-            st_v8(op + 8, &y[8]);
+            st_v8(e.out_f32 + f32_off(a.p, a.c, a.C), &y[0]);
+            st_v8(e.out_f32 + f32_off(a.p, a.c + 8, a.C), &y[8]);
         } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-                if (j < nv) op[j] = y[j];
+                if (j < nv) e.out_f32[f32_off(a.p, a.c + j, a.C)] = y[j];
         }
     }
 }
@@ -943,12 +972,12 @@ __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int
         }
         if (e.post != 0) {
             for (int b = 0; b < nv; ++b) {
-                y[b] = __fadd_rn(y[b], e.residual[p * C + c0 + b]);
+                y[b] = __fadd_rn(y[b], e.residual[f32_off(p, c0 + b, C)]);
                 if (e.post == 1) y[b] = fmaxf(y[b], 0.0f);
             }
         }
         if (e.out_f32)
-            for (int b = 0; b < nv; ++b) e.out_f32[p * C + c0 + b] = y[b];
+            for (int b = 0; b < nv; ++b) e.out_f32[f32_off(p, c0 + b, C)] = y[b];
         const size_t pq = (static_cast<size_t>(n) * (OH + 2) + oh + 1) * (OW + 2) + ow + 1;
         if (e.out_q0)
             for (int b = 0; b < nv; ++b) e.out_q0[pq * e.ldq0 + c0 + b] = sat8(quant_code(y[b], e.inv0, e.s0));
@@ -959,7 +988,7 @@ __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int
 
 // ------------------------------------------------------------------ stem maxpool
 
-// 3x3/s2/p1 maxpool (padding never wins) of fp32 NHWC [N][H][W][C]; writes the
+// 3x3/s2/p1 maxpool (padding never wins) of an fp32 map [N][H][W][C]; writes the
 // pooled fp32 map and its (bordered) codes.  Quantization is monotone, so pooling the fp32
 // values and then quantizing equals the reference's order (ref_e2e.py:192-203).
 __global__ void maxpool_kernel(const float* __restrict__ in, int N, int H, int W, int C, int OH, int OW,
@@ -979,10 +1008,10 @@ __global__ void maxpool_kernel(const float* __restrict__ in, int N, int H, int W
             for (int j = 0; j < 3; ++j) {
                 const int iw = ow * 2 + j - 1;
                 if (iw < 0 || iw >= W) continue;
-                m = fmaxf(m, in[((static_cast<size_t>(n) * H + ih) * W + iw) * C + c]);
+                m = fmaxf(m, in[f32_off((static_cast<size_t>(n) * H + ih) * W + iw, c, C)]);
             }
         }
-        if (e.out_f32) e.out_f32[p * C + c] = m;
+        if (e.out_f32) e.out_f32[f32_off(p, c, C)] = m;
         const size_t pq = (static_cast<size_t>(n) * (OH + 2) + oh + 1) * (OW + 2) + ow + 1;
         if (e.out_q0) e.out_q0[pq * e.ldq0 + c] = sat8(quant_code(m, e.inv0, e.s0));
         if (e.out_q1) e.out_q1[pq * e.ldq1 + c] = sat8(quant_code(m, e.inv1, e.s1));
@@ -1019,10 +1048,10 @@ __global__ void head_kernel(const float* __restrict__ x, int HW, int C, const fl
                             const float* __restrict__ fc_b, int n_out, float* __restrict__ logits) {
     extern __shared__ float pooled[];
     const int n = blockIdx.x;
-    const float* xn = x + static_cast<size_t>(n) * HW * C;
+    const size_t p0 = static_cast<size_t>(n) * HW;
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
         float s = 0.0f;
-        for (int p = 0; p < HW; ++p) s = __fadd_rn(s, xn[static_cast<size_t>(p) * C + c]);
+        for (int p = 0; p < HW; ++p) s = __fadd_rn(s, x[f32_off(p0 + p, c, C)]);
         pooled[c] = __fdiv_rn(s, static_cast<float>(HW));
     }
     __syncthreads();
