@@ -95,6 +95,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     }
 }
 
+// The same wait by every lane of a converged warp; the result is made warp-uniform.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity) {
+    const bool ok = mbar_wait(bar, parity);
+    return __all_sync(0xffffffffu, ok);
+}
+
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
@@ -139,6 +145,41 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+// One lane of a converged warp (elect.sync) issues the MMA.  The issuing warp
+// runs its control loop with all 32 lanes: descriptors and counters stay
+// warp-uniform, and the issue keeps its pace while the epilogue warps that
+// share its scheduler are busy (a lone issuing lane inside a divergent branch
+// issued N=64 MMAs several times slower under that load).
+__device__ __forceinline__ void mma_i8_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_elect(uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(bar)
+        : "memory");
+}
+
+// True in exactly one lane of the converged warp.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, e;\n\t}\n"
+        : "=r"(pred));
+    return pred != 0;
 }
 
 // Arrive on an mbarrier once every previously issued tcgen05.mma of this thread completes.
@@ -626,35 +667,38 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int n_a = MODE == 1 ? g.n_cchunks : g.n_kchunks;   // A loads per tile
 
     if (warp == 0) {
-        if (lane == 0) {
-            // ---------------- TMA producer
-            uint32_t last_ph = 0;   // bit s: parity of the last load issued into stage s
-            uint32_t used = 0;      // bit s: stage s received at least one load
-            bool ok = true;
-            if (g.b_resident) {
+        // ---------------- TMA producer (whole warp; one elected lane issues the copies)
+        uint32_t last_ph = 0;   // bit s: parity of the last load issued into stage s
+        uint32_t used = 0;      // bit s: stage s received at least one load
+        bool ok = true;
+        if (g.b_resident) {
+            if (elect_one()) {
                 mbar_expect_tx(bfull, g.b_bytes * g.n_kchunks);
                 for (int kc = 0; kc < g.n_kchunks; ++kc)
                     tma_load_2d(smem_u32(sB + kc * sb_stride), &map_b, bfull, kc * CB, nt * BN);
             }
-            int s = 0;
-            uint32_t ph = 0;
-            for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
-                int w0 = 0, h0 = 0, n0 = 0;
-                if (g.mode == 0) {
-                    const int tw_i = mt % g.tiles_w;
-                    const int rest = mt / g.tiles_w;
-                    w0 = tw_i * g.TW;
-                    h0 = (rest % g.tiles_h) * g.TH;
-                    n0 = (rest / g.tiles_h) * g.TN;
+            __syncwarp();
+        }
+        int s = 0;
+        uint32_t ph = 0;
+        for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
+            int w0 = 0, h0 = 0, n0 = 0;
+            if (g.mode == 0) {
+                const int tw_i = mt % g.tiles_w;
+                const int rest = mt / g.tiles_w;
+                w0 = tw_i * g.TW;
+                h0 = (rest % g.tiles_h) * g.TH;
+                n0 = (rest / g.tiles_h) * g.TN;
+            }
+            int tap = 0, cc = 0;
+            for (int ka = 0; ka < n_a; ++ka) {
+                if (!mbar_wait_warp(empty0 + 8 * s, ph ^ 1)) {
+                    if (lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
+                    ok = false;
+                    break;
                 }
-                int tap = 0, cc = 0;
-                for (int ka = 0; ka < n_a; ++ka) {
-                    if (!mbar_wait(empty0 + 8 * s, ph ^ 1)) {
-                        atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t fb = full0 + 8 * s;
+                const uint32_t fb = full0 + 8 * s;
+                if (elect_one()) {
                     mbar_expect_tx(fb, g.a_bytes + (g.b_resident ? 0u : g.b_bytes));
                     if (MODE == 1) {
                         tma_load_2d(smem_u32(sA + s * g.a_stage), &map_a, fb, ka * CB, mt * 128 + g.blk_off);
@@ -665,86 +709,84 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                                     w0 * g.SW + kj - g.PW + g.coord_off, h0 * g.SH + ki - g.PH + g.coord_off, n0);
                         if (!g.b_resident) tma_load_2d(smem_u32(sB + s * sb_stride), &map_b, fb, ka * CB, nt * BN);
                     }
-                    last_ph = (last_ph & ~(1u << s)) | (ph << s);
-                    used |= 1u << s;
-                    if (++cc == g.n_cchunks) { cc = 0; ++tap; }
-                    if (++s == S) { s = 0; ph ^= 1; }
                 }
+                __syncwarp();
+                last_ph = (last_ph & ~(1u << s)) | (ph << s);
+                used |= 1u << s;
+                if (++cc == g.n_cchunks) { cc = 0; ++tap; }
+                if (++s == S) { s = 0; ph ^= 1; }
             }
-            // Every issued copy must have landed before the CTA exits.
-            for (int st = 0; st < S; ++st)
-                if ((used >> st) & 1u)
-                    if (!mbar_wait(full0 + 8 * st, (last_ph >> st) & 1u)) {
-                        atomicExch(&g_ptq8_error, ERR_DRAIN);
-                        break;
-                    }
-            if (g.b_resident && !mbar_wait(bfull, 0)) atomicExch(&g_ptq8_error, ERR_DRAIN);
         }
+        // Every issued copy must have landed before the CTA exits.
+        for (int st = 0; st < S; ++st)
+            if ((used >> st) & 1u)
+                if (!mbar_wait_warp(full0 + 8 * st, (last_ph >> st) & 1u)) {
+                    if (lane == 0) atomicExch(&g_ptq8_error, ERR_DRAIN);
+                    break;
+                }
+        if (g.b_resident && !mbar_wait_warp(bfull, 0) && lane == 0) atomicExch(&g_ptq8_error, ERR_DRAIN);
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer
-            const uint32_t idesc = make_idesc_i8(BN);
-            // descriptors of stage 0 / B chunk 0; other stages, taps and chunks only move the
-            // start address (16-byte units).  The issue loop is kept to register adds: the
-            // tensor core takes small MMAs as fast as this thread can issue them.
-            const uint64_t adesc0 = make_sdesc(smem_u32(sA), CB);
-            const uint64_t bdesc0 = make_sdesc(smem_u32(sB), CB);
-            const uint64_t a_row_step = static_cast<uint64_t>((g.Wp * CB) >> 4);      // mode 1: next kernel row
-            const uint64_t b_tap_step = static_cast<uint64_t>((g.n_cchunks * sb_stride) >> 4);
-            const uint64_t a_stage_step = static_cast<uint64_t>(g.a_stage >> 4);
-            const uint64_t b_chunk_step = static_cast<uint64_t>(sb_stride >> 4);
-            bool ok = !g.b_resident || mbar_wait(bfull, 0);
-            if (!ok) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
-            int s = 0;
-            uint32_t ph = 0;
-            int t = 0;
-            for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x, ++t) {
-                const int buf = t % NA;
-                const uint32_t use = static_cast<uint32_t>(t / NA);
-                if (!mbar_wait(acce0 + 8 * buf, (use & 1u) ^ 1u)) {
-                    atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
+        // ---------------- MMA issuer (whole warp; one elected lane issues each MMA)
+        const uint32_t idesc = make_idesc_i8(BN);
+        // descriptors of stage 0 / B chunk 0; other stages, taps and chunks only move the
+        // start address (16-byte units), so the issue loop is register adds.
+        const uint64_t adesc0 = make_sdesc(smem_u32(sA), CB);
+        const uint64_t bdesc0 = make_sdesc(smem_u32(sB), CB);
+        const uint64_t a_row_step = static_cast<uint64_t>((g.Wp * CB) >> 4);      // mode 1: next kernel row
+        const uint64_t b_tap_step = static_cast<uint64_t>((g.n_cchunks * sb_stride) >> 4);
+        const uint64_t a_stage_step = static_cast<uint64_t>(g.a_stage >> 4);
+        const uint64_t b_chunk_step = static_cast<uint64_t>(sb_stride >> 4);
+        bool ok = !g.b_resident || mbar_wait_warp(bfull, 0);
+        if (!ok && lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+        int s = 0;
+        uint32_t ph = 0;
+        int buf = 0;
+        uint32_t use_ph = 0;   // parity of the current use of accumulator `buf`
+        for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
+            if (!mbar_wait_warp(acce0 + 8 * buf, use_ph ^ 1u)) {
+                if (lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + static_cast<uint32_t>(buf * g.acc_cols);
+            for (int ka = 0; ka < n_a; ++ka) {
+                if (!mbar_wait_warp(full0 + 8 * s, ph)) {
+                    if (lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+                    ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem + static_cast<uint32_t>(buf * g.acc_cols);
-                for (int ka = 0; ka < n_a; ++ka) {
-                    if (!mbar_wait(full0 + 8 * s, ph)) {
-                        atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint64_t da0 = adesc0 + static_cast<uint64_t>(s) * a_stage_step;
-                    if (MODE == 1) {
-                        uint64_t da_row = da0;
-                        uint64_t db = bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step;
-                        uint32_t acc = ka != 0 ? 1u : 0u;
-                        for (int i = 0; i < g.KH; ++i, da_row += a_row_step) {
-                            uint64_t da = da_row;
-                            for (int j = 0; j < g.KW; ++j, da += static_cast<uint64_t>(CB >> 4), db += b_tap_step) {
+                const uint64_t da0 = adesc0 + static_cast<uint64_t>(s) * a_stage_step;
+                if (MODE == 1) {
+                    uint64_t da_row = da0;
+                    uint64_t db = bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step;
+                    uint32_t acc = ka != 0 ? 1u : 0u;
+                    for (int i = 0; i < g.KH; ++i, da_row += a_row_step) {
+                        uint64_t da = da_row;
+                        for (int j = 0; j < g.KW; ++j, da += static_cast<uint64_t>(CB >> 4), db += b_tap_step) {
 #pragma unroll
-                                for (int k = 0; k < CB / 32; ++k) {
-                                    mma_i8(d, da + 2 * k, db + 2 * k, idesc, acc);
-                                    acc = 1u;
-                                }
+                            for (int k = 0; k < CB / 32; ++k) {
+                                mma_i8_elect(d, da + 2 * k, db + 2 * k, idesc, acc);
+                                acc = 1u;
                             }
                         }
-                    } else {
-                        const uint64_t db = bdesc0 + static_cast<uint64_t>(g.b_resident ? ka : s) * b_chunk_step;
-#pragma unroll
-                        for (int k = 0; k < CB / 32; ++k)
-                            mma_i8(d, da0 + 2 * k, db + 2 * k, idesc, (ka | k) != 0 ? 1u : 0u);
                     }
-                    mma_commit(empty0 + 8 * s);
-                    if (++s == S) { s = 0; ph ^= 1; }
+                } else {
+                    const uint64_t db = bdesc0 + static_cast<uint64_t>(g.b_resident ? ka : s) * b_chunk_step;
+#pragma unroll
+                    for (int k = 0; k < CB / 32; ++k)
+                        mma_i8_elect(d, da0 + 2 * k, db + 2 * k, idesc, (ka | k) != 0 ? 1u : 0u);
                 }
-                if (!ok) break;
-                mma_commit(accf0 + 8 * buf);
+                mma_commit_elect(empty0 + 8 * s);
+                if (++s == S) { s = 0; ph ^= 1; }
             }
-            // all MMAs of this thread complete before TMEM can be released
-            mma_commit(donebar);
-            if (!mbar_wait(donebar, 0)) atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
+            if (!ok) break;
+            mma_commit_elect(accf0 + 8 * buf);
+            if (++buf == NA) { buf = 0; use_ph ^= 1u; }
         }
+        // all MMAs of this warp complete before TMEM can be released
+        mma_commit_elect(donebar);
+        if (!mbar_wait_warp(donebar, 0) && lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
     } else {
         // ---------------- epilogue: TMEM lanes 32*(warp%4) .. +31 = tile rows.
         // Warps form NA groups; group gi drains accumulator gi, i.e. tiles t = gi (mod NA),
