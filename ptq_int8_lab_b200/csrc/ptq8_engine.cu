@@ -520,8 +520,10 @@ int acc_cols_for(int bn) {
     return tc;
 }
 
-// Accumulator buffers in TMEM (512 columns): 4 when they fit, else 2.
-int n_acc_for(int bn) { return 4 * acc_cols_for(bn) <= 512 ? 4 : 2; }
+// Accumulator buffers in TMEM (512 columns): 8 of <= 64 columns, 4 of 128, 2 of 256.
+// The epilogue has min(4, buffers) warp groups; each owns every n_groups-th buffer.
+int n_acc_for(int bn) { return std::min(8, 512 / acc_cols_for(bn)); }
+int n_groups_for(int bn) { return std::min(4, n_acc_for(bn)); }
 
 int finalize(ptq8_engine* e, int max_batch) {
     const Model& m = *e->model;
@@ -817,6 +819,7 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.BN = st.bn;
     g.acc_cols = acc_cols_for(st.bn);
     g.n_acc = n_acc_for(st.bn);
+    g.n_groups = n_groups_for(st.bn);
     g.stages = st.stages;
     g.b_resident = st.b_resident;
     g.b_bytes = (uint32_t)(st.bn * st.cb);

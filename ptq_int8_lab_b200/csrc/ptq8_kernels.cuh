@@ -575,7 +575,8 @@ struct ConvGeom {
     int n_cchunks, n_kchunks;   // channel chunks per tap, total K chunks
     int BN;                     // N tile (multiple of 16, <= 256)
     int acc_cols;               // TMEM columns per accumulator buffer (power of two >= max(32, BN))
-    int n_acc;                  // accumulator buffers (2 or 4): tiles in flight between MMA and epilogue
+    int n_acc;                  // accumulator buffers (2, 4 or 8): tiles in flight between MMA and epilogue
+    int n_groups;               // epilogue warp groups (2 or 4); group gi drains buffers gi, gi + n_groups, ...
     int stages;                 // A (and streamed B) pipeline depth, <= kMaxStages
     int b_resident;             // 1: the CTA's whole weight slab stays in shared memory
     uint32_t a_bytes, b_bytes;  // TMA bytes per A stage / per B chunk
@@ -604,7 +605,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                const ConvGeom g, const EpiParams e) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_abort;
-    __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 10];  // a_full, a_empty, b_full, acc_full[4], acc_empty[4], done
+    __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 18];  // a_full, a_empty, b_full, acc_full[8], acc_empty[8], done
     __shared__ uint32_t tslot;
     // A wait of an earlier CTA already ran out: skip the work (block-uniform decision).
     if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile int*>(&g_ptq8_error);
@@ -628,10 +629,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const uint32_t empty0 = smem_u32(&bars[kMaxStages]);
     const uint32_t bfull = smem_u32(&bars[2 * kMaxStages]);
     const uint32_t accf0 = smem_u32(&bars[2 * kMaxStages + 1]);
-    const uint32_t acce0 = smem_u32(&bars[2 * kMaxStages + 5]);
-    const uint32_t donebar = smem_u32(&bars[2 * kMaxStages + 9]);
+    const uint32_t acce0 = smem_u32(&bars[2 * kMaxStages + 9]);
+    const uint32_t donebar = smem_u32(&bars[2 * kMaxStages + 17]);
     const int NA = g.n_acc;
-    const int group_warps = kEpiWarps / NA;   // epilogue warps per accumulator buffer (multiple of 4)
+    const int NG = g.n_groups;
+    const int group_warps = kEpiWarps / NG;   // epilogue warps per group (multiple of 4)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -789,8 +791,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (!mbar_wait_warp(donebar, 0) && lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
     } else {
         // ---------------- epilogue: TMEM lanes 32*(warp%4) .. +31 = tile rows.
-        // Warps form NA groups; group gi drains accumulator gi, i.e. tiles t = gi (mod NA),
-        // so NA tiles are in flight.  Inside a group the warps of a quadrant take
+        // Warps form NG groups; group gi takes tiles t = gi (mod NG), held in accumulator
+        // t % NA, so NA tiles are in flight.  Inside a group the warps of a quadrant take
         // interleaved 16-column groups.
         const int ew = warp - 2;
         const int gi = ew / group_warps;
@@ -807,8 +809,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         // codes can only saturate low when the values are not already clipped at zero
         const bool lower = RES ? e.post != 1 : e.act == 0;
         int t = gi;
-        for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NA * gridDim.x, t += NA) {
-            const int buf = gi;
+        for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NG * gridDim.x, t += NG) {
+            const int buf = t % NA;
             const uint32_t use = static_cast<uint32_t>(t / NA);
             int n, h, w;
             bool valid;
