@@ -101,8 +101,14 @@ struct Step {
     int8_t* d_w = nullptr;
     float* d_factor = nullptr;
     float* d_bias = nullptr;
-    int8_t* d_im2col = nullptr;   // stem rows
+    int8_t* d_im2col = nullptr;   // stem rows, bordered [N][OH+2][OW+2][kpad]
     CUtensorMap map_a{}, map_b{};
+    // aux GEMM: this conv recomputes its residual (the stem's output) from the
+    // stem's im2col rows instead of reading a stored fp32 map
+    int aux_src = -1;      // step index of the stem, -1 none
+    int aux_off = 0;       // byte offset of the aux tile inside an A stage
+    int acc_cols = 0;      // TMEM columns per accumulator buffer (main + aux)
+    CUtensorMap map_xa{}, map_xb{};
 };
 
 struct ConvQ {   // quantized conv after graph passes
@@ -326,6 +332,24 @@ void choose_bn(int cout, int* bn, int* ntiles) {
     *bn = b;
 }
 
+// Whether the block conv `ci`, whose residual is the stem's output, can recompute
+// that residual from the stem's im2col rows (one K = 32 GEMM in its own kernel)
+// instead of reading it as a stored fp32 map: a 3x3 stride-1 "same" conv on the
+// stem's map (halo-block mode), N tile = all channels, same channel count.
+bool stem_identity_fusable(const ptq8_engine* e, int ci) {
+    const Model& m = *e->model;
+    if (m.stem_pool) return false;
+    const ConvSpec& st = e->q[0].spec;
+    const ConvSpec& c = e->q[ci].spec;
+    if (st.cin * st.kh * st.kw > 32 || st.groups != 1) return false;
+    if (e->q[ci].view_oh > 0 || c.groups != 1 || c.kh != 3 || c.kw != 3 || c.sh != 1 || c.sw != 1 || c.ph != 1 ||
+        c.pw != 1)
+        return false;
+    if (c.cout != st.cout || c.cout > 128 || c.cout % 16 != 0 || round_up(c.cin, 32) % 64 != 0) return false;
+    const int oh = conv_out_dim(e->in_h, st.kh, st.sh, st.ph), ow = conv_out_dim(e->in_w, st.kw, st.sw, st.pw);
+    return oh * ow >= 64 && 128 + 2 * (ow + 2) + 2 <= 256;
+}
+
 int plan(ptq8_engine* e) {
     const Model& m = *e->model;
     e->vals.clear();
@@ -381,6 +405,7 @@ int plan(ptq8_engine* e) {
     int cur = -1;
     int rc = add_conv(0, 0, &cur, -1, 0);
     if (rc) return rc;
+    const int stem_val = cur, stem_step = (int)e->steps.size() - 1;
     if (m.stem_pool) {
         Value& v0 = e->vals[cur];
         v0.need_f32 = true;
@@ -401,6 +426,7 @@ int plan(ptq8_engine* e) {
         for (int ci : b.convs)
             if (ci >= 0) cs.push_back(ci);
         int ident = -1;
+        bool fuse = false;
         if (b.residual != 0) {
             if (b.ds >= 0) {
                 int dv;
@@ -410,7 +436,8 @@ int plan(ptq8_engine* e) {
             } else {
                 ident = cur;
             }
-            e->vals[ident].need_f32 = true;
+            fuse = ident == stem_val && !cs.empty() && stem_identity_fusable(e, cs.back());
+            if (!fuse) e->vals[ident].need_f32 = true;
         }
         int t = cur;
         for (size_t k = 0; k < cs.size(); ++k) {
@@ -418,6 +445,7 @@ int plan(ptq8_engine* e) {
             int ov;
             rc = add_conv(cs[k], t, &ov, last && b.residual ? ident : -1, last ? b.residual : 0);
             if (rc) return rc;
+            if (last && fuse) e->steps.back().aux_src = stem_step;
             t = ov;
         }
         cur = t;
@@ -453,10 +481,18 @@ constexpr size_t kSmemBudget = 225 * 1024;
 // conv_tc_kernel specializations: [K-chunk 32/64/128][mode][code outputs][residual][fp32 out]
 void* g_conv_table[3][2][3][2][2];
 
+// the same with the aux GEMM (mode 1, residual): [K-chunk 64/128][code outputs 1/2][fp32 out]
+void* g_conv_aux_table[2][2][2];
+
 template <int CBI, int MODE, int NOUT, int RES, int F32>
 void fill_one() {
     g_conv_table[CBI][MODE][NOUT][RES][F32] =
-        reinterpret_cast<void*>(&conv_tc_kernel<(32 << CBI), MODE, NOUT, RES != 0, F32 != 0>);
+        reinterpret_cast<void*>(&conv_tc_kernel<(32 << CBI), MODE, NOUT, RES != 0, F32 != 0, false>);
+}
+template <int CBI, int NOUT, int F32>
+void fill_aux() {
+    g_conv_aux_table[CBI - 1][NOUT - 1][F32] =
+        reinterpret_cast<void*>(&conv_tc_kernel<(32 << CBI), 1, NOUT, true, F32 != 0, true>);
 }
 template <int CBI, int MODE, int NOUT, int RES>
 void fill_f32() { fill_one<CBI, MODE, NOUT, RES, 0>(); fill_one<CBI, MODE, NOUT, RES, 1>(); }
@@ -472,15 +508,20 @@ void fill_table() {
     fill_mode<0>();
     fill_mode<1>();
     fill_mode<2>();
+    fill_aux<1, 1, 0>(); fill_aux<1, 1, 1>(); fill_aux<1, 2, 0>(); fill_aux<1, 2, 1>();
+    fill_aux<2, 1, 0>(); fill_aux<2, 1, 1>(); fill_aux<2, 2, 0>(); fill_aux<2, 2, 1>();
     done = true;
 }
 
 int cb_index(int cb) { return cb == 128 ? 2 : (cb == 64 ? 1 : 0); }
 
-// Dynamic shared memory of conv_tc_kernel for a pipeline shape.
-size_t conv_smem_bytes(int a_stage, int cb, int bn, int stages, int b_chunks) {
+// Dynamic shared memory of conv_tc_kernel for a pipeline shape (aux: + aux weights
+// [bn][32] and their dequantization constants).
+size_t conv_smem_bytes(int a_stage, int cb, int bn, int stages, int b_chunks, bool aux = false) {
     const size_t sb = (size_t)round_up(bn * cb, 1024);
-    return 1024 + (size_t)stages * a_stage + (size_t)b_chunks * sb + 8 * (size_t)round_up(bn, 32);
+    const size_t fb = 8 * (size_t)round_up(bn, 32);
+    return 1024 + (size_t)stages * a_stage + (size_t)b_chunks * sb + fb +
+           (aux ? (size_t)round_up(bn * 32, 1024) + fb : 0);
 }
 
 // Keep the whole weight slab of the N tile resident when it fits next to a
@@ -490,7 +531,7 @@ bool choose_pipeline(Step& st, int min_res) {
     for (int S : {24, 20, 16, 12, 10, 8, 6, 5, 4, 3, 2}) {
         if (S < min_res) break;
         if ((size_t)S * st.a_stage > 96 * 1024 && S > min_res) continue;   // ~96 KB of A in flight is plenty
-        const size_t b = conv_smem_bytes(st.a_stage, st.cb, st.bn, S, st.n_kchunks);
+        const size_t b = conv_smem_bytes(st.a_stage, st.cb, st.bn, S, st.n_kchunks, st.aux_src >= 0);
         if (b <= kSmemBudget) {
             st.stages = S;
             st.b_resident = 1;
@@ -520,10 +561,11 @@ int acc_cols_for(int bn) {
     return tc;
 }
 
-// Accumulator buffers in TMEM (512 columns): 8 of <= 64 columns, 4 of 128, 2 of 256.
-// The epilogue has min(4, buffers) warp groups; each owns every n_groups-th buffer.
-int n_acc_for(int bn) { return std::min(8, 512 / acc_cols_for(bn)); }
-int n_groups_for(int bn) { return std::min(4, n_acc_for(bn)); }
+// Accumulator buffers in TMEM (512 columns) of `cols` columns each: 8 of <= 64
+// columns, 4 of 128, 2 of 256.  The epilogue has min(4, buffers) warp groups; each
+// owns every n_groups-th buffer.
+int n_acc_for(int cols) { return std::min(8, 512 / cols); }
+int n_groups_for(int cols) { return std::min(4, n_acc_for(cols)); }
 
 int finalize(ptq8_engine* e, int max_batch) {
     const Model& m = *e->model;
@@ -599,7 +641,10 @@ int finalize(ptq8_engine* e, int max_batch) {
                         for (int j = 0; j < c.kw; ++j)
                             w[(size_t)o * st.ktot + (i * c.kw + j) * c.cin + ci] =
                                 cq.codes[(((size_t)o * c.cin + ci) * c.kh + i) * c.kw + j];
-            if (!e->dalloc(&st.d_im2col, NB * st.oh * st.ow * st.kpad, "alloc im2col")) return PTQ8_ERR_CUDA;
+            const size_t rows = NB * (st.oh + 2) * (st.ow + 2);
+            if (!e->dalloc(&st.d_im2col, rows * st.kpad, "alloc im2col") ||
+                !e->cuda_ok(cudaMemset(st.d_im2col, 0, rows * st.kpad), "clear im2col"))
+                return PTQ8_ERR_CUDA;
         } else {
             cpad = round_up(c.cin, 32);
             st.ktot = c.kh * c.kw * cpad;
@@ -638,9 +683,16 @@ int finalize(ptq8_engine* e, int max_batch) {
             if (st.blk_rows <= 256) {
                 st.mode = 1;
                 st.a_stage = round_up(st.blk_rows * st.cb, 1024);
+                if (st.aux_src >= 0) {   // + the aux tile: 128 im2col rows of 32 bytes
+                    st.aux_off = st.a_stage;
+                    st.a_stage += 128 * 32;
+                }
                 if (!choose_pipeline(st, 2)) st.mode = 0;
             }
         }
+        if (st.aux_src >= 0 && (st.mode != 1 || st.n_ntiles != 1 || (st.cb != 64 && st.cb != 128)))
+            return e->fail(strf("conv[%d]: stem identity fusion needs the halo-block pipeline", st.conv));
+        st.acc_cols = acc_cols_for(st.bn) * (st.aux_src >= 0 ? 2 : 1);
         if (st.mode == 0) {
             st.a_stage = 128 * st.cb;
             choose_pipeline(st, 4);
@@ -648,10 +700,10 @@ int finalize(ptq8_engine* e, int max_batch) {
         if (st.smem > kSmemBudget)
             return e->fail(strf("conv[%d]: no pipeline fits in shared memory", st.conv));
         if (st.kind == K_STEM_IM2COL) {
-            // the im2col rows form a [N][OH][OW][kpad] map read as a 1x1 conv
-            cuuint64_t dims[4] = {(cuuint64_t)st.kpad, (cuuint64_t)st.ow, (cuuint64_t)st.oh, (cuuint64_t)max_batch};
-            cuuint64_t strides[3] = {(cuuint64_t)st.kpad, (cuuint64_t)st.kpad * st.ow,
-                                     (cuuint64_t)st.kpad * st.ow * st.oh};
+            // the im2col rows form a bordered [N][OH+2][OW+2][kpad] map read as a 1x1 conv
+            const cuuint64_t hp = st.oh + 2, wp = st.ow + 2;
+            cuuint64_t dims[4] = {(cuuint64_t)st.kpad, wp, hp, (cuuint64_t)max_batch};
+            cuuint64_t strides[3] = {(cuuint64_t)st.kpad, (cuuint64_t)st.kpad * wp, (cuuint64_t)st.kpad * wp * hp};
             cuuint32_t box[4] = {(cuuint32_t)st.cb, (cuuint32_t)st.TW, (cuuint32_t)st.TH, (cuuint32_t)st.TN};
             cuuint32_t estr[4] = {1, 1, 1, 1};
             if (!make_map(e, &st.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, st.d_im2col, dims, strides, box, estr,
@@ -668,6 +720,24 @@ int finalize(ptq8_engine* e, int max_batch) {
             if (!make_map(e, &st.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
                           swizzle_for(st.cb)))
                 return PTQ8_ERR_CUDA;
+            if (st.aux_src >= 0) {
+                // the stem's bordered im2col rows line up with this conv's bordered tile rows
+                const Step& src = e->steps[st.aux_src];
+                if (src.oh != vin.h || src.ow != vin.w || src.kpad != 32 || !src.d_im2col || !src.d_w)
+                    return e->fail(strf("conv[%d]: stem identity fusion geometry mismatch", st.conv));
+                cuuint64_t xdims[2] = {32, rows};
+                cuuint64_t xstr[1] = {32};
+                cuuint32_t xbox[2] = {32, 128};
+                if (!make_map(e, &st.map_xa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, src.d_im2col, xdims, xstr, xbox, estr,
+                              swizzle_for(32)))
+                    return PTQ8_ERR_CUDA;
+                cuuint64_t wdims[2] = {(cuuint64_t)src.ktot, (cuuint64_t)e->q[src.conv].spec.cout};
+                cuuint64_t wstr[1] = {(cuuint64_t)src.ktot};
+                cuuint32_t wbox[2] = {32, (cuuint32_t)st.bn};
+                if (!make_map(e, &st.map_xb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, src.d_w, wdims, wstr, wbox, estr,
+                              swizzle_for(32)))
+                    return PTQ8_ERR_CUDA;
+            }
         } else {
             const Value& vin = e->vals[st.in_val];
             int8_t* base = vin.codes[vin.code_index(st.s_in)];
@@ -694,13 +764,18 @@ int finalize(ptq8_engine* e, int max_batch) {
             const int nout = (int)out.scales.size();
             const int res = st.res_val >= 0 ? 1 : 0;
             const int f32 = out.need_f32 ? 1 : 0;
-            st.kfn = g_conv_table[cb_index(st.cb)][st.mode][nout][res][f32];
+            if (st.aux_src >= 0) {
+                if (nout < 1 || nout > 2) return e->fail(strf("conv[%d]: stem identity fusion needs 1-2 code outputs", st.conv));
+                st.kfn = g_conv_aux_table[cb_index(st.cb) - 1][nout - 1][f32];
+            } else {
+                st.kfn = g_conv_table[cb_index(st.cb)][st.mode][nout][res][f32];
+            }
             if (!e->cuda_ok(cudaFuncSetAttribute(st.kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget),
                             "smem attr"))
                 return PTQ8_ERR_CUDA;
             int occ = 1;
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, st.kfn, kConvThreads, st.smem);
-            const int occ_tmem = 512 / (n_acc_for(st.bn) * acc_cols_for(st.bn));
+            const int occ_tmem = 512 / (n_acc_for(st.acc_cols) * st.acc_cols);
             occ = std::max(1, std::min(occ, occ_tmem));
             st.grid_x = std::max(1, sms * occ / st.n_ntiles);
         }
@@ -797,7 +872,7 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.KH = st.kind == K_STEM_IM2COL ? 1 : st.kh;
     if (st.kind == K_STEM_IM2COL) {
         g.KW = 1; g.KH = 1; g.SH = 1; g.SW = 1; g.PH = 0; g.PW = 0;
-        g.coord_off = 0;
+        g.coord_off = 1;   // bordered im2col map
         g.n_cchunks = st.kpad / st.cb;
     } else {
         g.KW = st.kw; g.SH = st.sh; g.SW = st.sw; g.PH = st.ph; g.PW = st.pw;
@@ -817,15 +892,24 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.a_stage = st.a_stage;
     g.n_kchunks = st.n_kchunks;
     g.BN = st.bn;
-    g.acc_cols = acc_cols_for(st.bn);
-    g.n_acc = n_acc_for(st.bn);
-    g.n_groups = n_groups_for(st.bn);
+    g.acc_cols = st.acc_cols;
+    g.n_acc = n_acc_for(st.acc_cols);
+    g.n_groups = n_groups_for(st.acc_cols);
+    if (st.aux_src >= 0) {
+        const Step& src = e->steps[st.aux_src];
+        g.aux_off = st.aux_off;
+        g.aux_bytes = 128 * 32;
+        g.aux_col = acc_cols_for(st.bn);
+        ep.aux_factor = src.d_factor;
+        ep.aux_bias = src.d_bias;
+        ep.aux_act = src.act;
+    }
     g.stages = st.stages;
     g.b_resident = st.b_resident;
     g.b_bytes = (uint32_t)(st.bn * st.cb);
     dim3 grid((unsigned)std::min(g.m_tiles, st.grid_x), (unsigned)st.n_ntiles);
-    CUtensorMap ma = st.map_a, mb = st.map_b;
-    void* args[4] = {&ma, &mb, &g, &ep};
+    CUtensorMap ma = st.map_a, mb = st.map_b, mxa = st.map_xa, mxb = st.map_xb;
+    void* args[6] = {&ma, &mb, &mxa, &mxb, &g, &ep};
     cudaLaunchKernel(st.kfn, grid, dim3(kConvThreads), args, st.smem, s);
 }
 
@@ -848,7 +932,10 @@ void step_work(const ptq8_engine* e, int n, size_t si, double* macs, double* byt
     const Step& st = e->steps[si];
     const Value& out = e->vals[st.out_val];
     double outb = (double)n * out.h * out.w * out.c * ((out.need_f32 ? 4.0 : 0.0) + (double)out.scales.size());
-    double resb = st.res_val >= 0 ? (double)n * out.h * out.w * out.c * 4.0 : 0.0;
+    // residual: the stored fp32 map, or (aux GEMM) the stem's bordered im2col rows
+    double resb = st.res_val < 0 ? 0.0
+                  : st.aux_src >= 0 ? (double)n * (out.h + 2) * (out.w + 2) * 32.0
+                                    : (double)n * out.h * out.w * out.c * 4.0;
     *kind = st.kind;
     if (st.kind == K_MAXPOOL) {
         *macs = 0;
@@ -1377,9 +1464,14 @@ int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst,
     if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "sync")) return PTQ8_ERR_CUDA;
     if (what == 0) {
         const Step& st = e->steps[e->conv_step[index]];
-        if (st.kind == K_STEM_IM2COL) {
-            if (!e->cuda_ok(cudaMemcpy(host_dst, st.d_im2col, need, cudaMemcpyDeviceToHost), "dump"))
-                return PTQ8_ERR_CUDA;
+        if (st.kind == K_STEM_IM2COL) {   // drop the border rows of the bordered im2col map
+            const size_t row = (size_t)st.ow * st.kpad, prow = (size_t)(st.ow + 2) * st.kpad;
+            for (int i = 0; i < n; ++i) {
+                const int8_t* s0 = st.d_im2col + ((size_t)i * (st.oh + 2) + 1) * prow + st.kpad;
+                int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * st.oh * row;
+                if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, st.oh, cudaMemcpyDeviceToHost), "dump"))
+                    return PTQ8_ERR_CUDA;
+            }
             return PTQ8_OK;
         }
         const Value& v = e->vals[st.in_val];

@@ -436,6 +436,9 @@ struct EpiParams {
     int cout;
     int vec32;  // 1 when cout % 8 == 0: tiled fp32 maps, 256-bit loads/stores of 8 channels
     int act;    // activation of the conv itself: 0 none / 1 relu / 2 relu6
+    const float* aux_factor;   // AUX: dequantization of the aux accumulator (the residual)
+    const float* aux_bias;
+    int aux_act;
     int post;   // residual: 0 none, 1 add then relu, 2 add only
     // positional decomposition: channel c' = pos*dcr_oc + c of a 1x1 GEMM output is code
     // (pos / dcr_w, pos % dcr_w, c) of a dcr_h x dcr_w map (DepthToSpace, DCR order)
@@ -580,6 +583,13 @@ struct ConvGeom {
     int stages;                 // A (and streamed B) pipeline depth, <= kMaxStages
     int b_resident;             // 1: the CTA's whole weight slab stays in shared memory
     uint32_t a_bytes, b_bytes;  // TMA bytes per A stage / per B chunk
+    // aux GEMM (AUX kernels): a second 1x1 GEMM with K = 32 bytes per row, over
+    // rows aligned with the tile's rows, into a second accumulator; its
+    // dequantized output is the residual (a block identity recomputed instead
+    // of stored in fp32)
+    int aux_off;                // byte offset of the aux A tile (128 rows x 32 bytes) inside each A stage
+    uint32_t aux_bytes;         // TMA bytes of that tile
+    int aux_col;                // TMEM column of the aux accumulator inside a buffer
 };
 
 constexpr int kEpiWarps = 16;                      // 4 per TMEM lane quadrant
@@ -598,10 +608,12 @@ constexpr int kMaxStages = 24;
 //         i*Wp + j.  Border outputs are computed and dropped.
 // Template parameters fix the per-launch shape of the work so each launch runs
 // a lean instruction stream: CB = K-chunk bytes (swizzle width), MODE (above),
-// NOUT = int8 code outputs (0..2), RES = residual add, F32 = fp32 output.
-template <int CB, int MODE, int NOUT, bool RES, bool F32>
+// NOUT = int8 code outputs (0..2), RES = residual add, F32 = fp32 output,
+// AUX = the residual is the aux GEMM's output (map_xa / map_xb) instead of a load.
+template <int CB, int MODE, int NOUT, bool RES, bool F32, bool AUX>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+               const __grid_constant__ CUtensorMap map_xa, const __grid_constant__ CUtensorMap map_xb,
                const ConvGeom g, const EpiParams e) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_abort;
@@ -619,8 +631,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int sb_stride = (BN * CB + 1023) & ~1023;   // every B chunk 1024-byte aligned (swizzle atoms)
     uint8_t* sA = smem;
     uint8_t* sB = smem + S * g.a_stage;
-    float* s_factor = reinterpret_cast<float*>(sB + (g.b_resident ? g.n_kchunks : S) * sb_stride);
+    uint8_t* sBx = sB + (g.b_resident ? g.n_kchunks : S) * sb_stride;   // aux weights [BN][32] (AUX)
+    const int sbx_bytes = AUX ? (BN * 32 + 1023) & ~1023 : 0;
+    float* s_factor = reinterpret_cast<float*>(sBx + sbx_bytes);
     float* s_bias = s_factor + bn32;
+    float* s_afactor = s_bias + bn32;   // AUX
+    float* s_abias = s_afactor + bn32;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -649,6 +665,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         fence_mbar_init();
         tma_prefetch(&map_a);
         tma_prefetch(&map_b);
+        if (AUX) {
+            tma_prefetch(&map_xa);
+            tma_prefetch(&map_xb);
+        }
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(&tslot), NA * g.acc_cols);
@@ -660,6 +680,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const bool ok = c < BN && gc < e.cout;
             s_factor[c] = ok ? e.factor[gc] : 0.0f;
             s_bias[c] = ok ? e.bias[gc] : 0.0f;
+            if (AUX) {
+                s_afactor[c] = ok ? e.aux_factor[gc] : 0.0f;
+                s_abias[c] = ok ? e.aux_bias[gc] : 0.0f;
+            }
         }
     }
     tc_fence_before();
@@ -675,9 +699,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         bool ok = true;
         if (g.b_resident) {
             if (elect_one()) {
-                mbar_expect_tx(bfull, g.b_bytes * g.n_kchunks);
+                mbar_expect_tx(bfull, g.b_bytes * g.n_kchunks + (AUX ? static_cast<uint32_t>(BN * 32) : 0u));
                 for (int kc = 0; kc < g.n_kchunks; ++kc)
                     tma_load_2d(smem_u32(sB + kc * sb_stride), &map_b, bfull, kc * CB, nt * BN);
+                if (AUX) tma_load_2d(smem_u32(sBx), &map_xb, bfull, 0, nt * BN);
             }
             __syncwarp();
         }
@@ -701,7 +726,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
                 const uint32_t fb = full0 + 8 * s;
                 if (elect_one()) {
-                    mbar_expect_tx(fb, g.a_bytes + (g.b_resident ? 0u : g.b_bytes));
+                    const bool aux = AUX && ka == 0;
+                    mbar_expect_tx(fb, g.a_bytes + (g.b_resident ? 0u : g.b_bytes) + (aux ? g.aux_bytes : 0u));
+                    if (aux) tma_load_2d(smem_u32(sA + s * g.a_stage + g.aux_off), &map_xa, fb, 0, mt * 128);
                     if (MODE == 1) {
                         tma_load_2d(smem_u32(sA + s * g.a_stage), &map_a, fb, ka * CB, mt * 128 + g.blk_off);
                     } else {
@@ -738,6 +765,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const uint64_t b_tap_step = static_cast<uint64_t>((g.n_cchunks * sb_stride) >> 4);
         const uint64_t a_stage_step = static_cast<uint64_t>(g.a_stage >> 4);
         const uint64_t b_chunk_step = static_cast<uint64_t>(sb_stride >> 4);
+        const uint64_t xadesc0 = AUX ? make_sdesc(smem_u32(sA + g.aux_off), 32) : 0;
+        const uint64_t xbdesc = AUX ? make_sdesc(smem_u32(sBx), 32) : 0;
         bool ok = !g.b_resident || mbar_wait_warp(bfull, 0);
         if (!ok && lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
         int s = 0;
@@ -779,6 +808,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     for (int k = 0; k < CB / 32; ++k)
                         mma_i8_elect(d, da0 + 2 * k, db + 2 * k, idesc, (ka | k) != 0 ? 1u : 0u);
                 }
+                if (AUX && ka == 0)
+                    mma_i8_elect(d + static_cast<uint32_t>(g.aux_col), xadesc0 + static_cast<uint64_t>(s) * a_stage_step,
+                                 xbdesc, idesc, 0u);
                 mma_commit_elect(empty0 + 8 * s);
                 if (++s == S) { s = 0; ph ^= 1; }
             }
@@ -838,7 +870,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             float res[16];
             {
                 const int c0 = nt * BN + slice * 32;
-                if (RES && valid && slice < ncg && c0 < tile_end) load_res16(e, pf, c0, min(16, tile_end - c0), res);
+                if (RES && !AUX && valid && slice < ncg && c0 < tile_end)
+                    load_res16(e, pf, c0, min(16, tile_end - c0), res);
             }
             if (!mbar_wait(accf0 + 8 * buf, use & 1u)) {
                 atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
@@ -852,20 +885,22 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 uint32_t wq[2][8];                          // codes of both halves, per output
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
-                    uint32_t v[16];
+                    uint32_t v[16], vx[16];
                     __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the per-lane stores
                     tmem_ld16(trow + cg * 32 + hh * 16, v);
+                    if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + cg * 32 + hh * 16, vx);
                     tmem_wait_ld();
                     const int ch = c0 + hh * 16;
                     const int nv = min(16, tile_end - ch);
                     if (!valid || nv <= 0) continue;
                     float y[16];
                     dequant16(v, s_factor + cg * 32 + hh * 16, s_bias + cg * 32 + hh * 16, e.act, y);
+                    if (AUX) dequant16(vx, s_afactor + cg * 32 + hh * 16, s_abias + cg * 32 + hh * 16, e.aux_act, res);
                     finish16<RES, F32>(e, pf, ch, nv, y, res);
                     // prefetch the next residual half of this warp
                     {
                         const int cn = hh == 0 ? ch + 16 : c0 + 32 * kSlices;
-                        if (RES && (hh == 0 || cg + kSlices < ncg) && cn < tile_end)
+                        if (RES && !AUX && (hh == 0 || cg + kSlices < ncg) && cn < tile_end)
                             load_res16(e, pf, cn, min(16, tile_end - cn), res);
                     }
 #pragma unroll
@@ -905,7 +940,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 
 // ------------------------------------------------------------------ stem im2col
 
-// x: fp32 NCHW [N][C][H][W]; out: int8 [N*OH*OW][kpad] with k = (i*KW + j)*C + c,
+// x: fp32 NCHW [N][C][H][W]; out: int8 rows of a bordered [N][OH+2][OW+2][kpad]
+// map (border rows are never written and stay zero) with k = (i*KW + j)*C + c,
 // codes of the stem's scale, zero for out-of-image taps and k >= KH*KW*C.
 // One CTA per band of `rows` output rows of one image.  The input band is read
 // once (one warp per band row, coalesced) and quantized once into shared
@@ -950,11 +986,11 @@ __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restri
     }
     __syncthreads();
     const int npix = (r1 - r0) * OW;
-    int8_t* obase = out + (static_cast<size_t>(n) * OH + r0) * OW * kpad;
+    int8_t* obase = out + ((static_cast<size_t>(n) * (OH + 2) + r0 + 1) * (OW + 2) + 1) * kpad;
     for (int p = threadIdx.x; p < npix; p += blockDim.x) {
         const int ohl = p / OW, ow = p - (p / OW) * OW;
         const int8_t* bp = band + ohl * SH * band_w + ow * SW;
-        uint4* op = reinterpret_cast<uint4*>(obase + static_cast<size_t>(p) * kpad);
+        uint4* op = reinterpret_cast<uint4*>(obase + static_cast<size_t>(ohl * (OW + 2) + ow) * kpad);
         for (int k0 = 0; k0 < kpad; k0 += 16) {
             uint32_t wv[4];
 #pragma unroll
