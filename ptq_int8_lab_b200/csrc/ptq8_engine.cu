@@ -675,7 +675,8 @@ int finalize(ptq8_engine* e, int max_batch) {
         st.n_kchunks = st.kind == K_STEM_IM2COL ? st.kpad / st.cb : st.kh * st.kw * (cpad / st.cb);
         // mode 1: stride-1 "same" convs read one halo block per tile (needs resident weights)
         st.mode = 0;
-        if (st.kind == K_TC && cq.view_oh == 0 && st.kh == st.kw && st.kh > 1 && st.sh == 1 && st.sw == 1 &&
+        // (the kernel's halo-block MMA loop is compiled for 3x3)
+        if (st.kind == K_TC && cq.view_oh == 0 && st.kh == 3 && st.kw == 3 && st.sh == 1 && st.sw == 1 &&
             st.ph == (st.kh - 1) / 2 && st.pw == st.ph && st.ph <= 1 && st.oh == st.ih && st.ow == st.iw &&
             st.oh * st.ow >= 64) {
             const int wp = st.iw + 2;

@@ -163,6 +163,51 @@ __device__ __forceinline__ void mma_i8_elect(uint32_t d_tmem, uint64_t a_desc, u
         : "memory");
 }
 
+// The KS = CB/32 MMAs of one K chunk (K offsets 0, 32, 64, 96 bytes: descriptor
+// start +2 per 32 bytes) in one asm block: one election and one accumulate
+// predicate per chunk, one 64-bit add per further MMA.
+template <int KS>
+__device__ __forceinline__ void mma_chunk_elect(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    static_assert(KS == 1 || KS == 2 || KS == 4, "K chunk of 32, 64 or 128 bytes");
+    if constexpr (KS == 1) {
+        asm volatile(
+            "{\n\t.reg .pred e, p;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+            "l"(da), "l"(db), "r"(idesc), "r"(acc)
+            : "memory");
+    } else if constexpr (KS == 2) {
+        asm volatile(
+            "{\n\t.reg .pred e, p;\n\t.reg .b64 a1, b1;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t"
+            "add.s64 a1, %1, 2;\n\t"
+            "add.s64 b1, %2, 2;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::i8 [%0], a1, b1, %3, 1;\n\t}\n" ::"r"(d),
+            "l"(da), "l"(db), "r"(idesc), "r"(acc)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred e, p;\n\t.reg .b64 a1, b1, a2, b2, a3, b3;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t"
+            "add.s64 a1, %1, 2;\n\t"
+            "add.s64 b1, %2, 2;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::i8 [%0], a1, b1, %3, 1;\n\t"
+            "add.s64 a2, %1, 4;\n\t"
+            "add.s64 b2, %2, 4;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::i8 [%0], a2, b2, %3, 1;\n\t"
+            "add.s64 a3, %1, 6;\n\t"
+            "add.s64 b3, %2, 6;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::i8 [%0], a3, b3, %3, 1;\n\t}\n" ::"r"(d),
+            "l"(da), "l"(db), "r"(idesc), "r"(acc)
+            : "memory");
+    }
+}
+
 __device__ __forceinline__ void mma_commit_elect(uint32_t bar) {
     asm volatile(
         "{\n\t.reg .pred e;\n\t"
@@ -789,24 +834,21 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 tc_fence_after();
                 const uint64_t da0 = adesc0 + static_cast<uint64_t>(s) * a_stage_step;
                 if (MODE == 1) {
+                    // 3x3 taps (mode 1 is planned only for 3x3 convs), fully unrolled
                     uint64_t da_row = da0;
                     uint64_t db = bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step;
                     uint32_t acc = ka != 0 ? 1u : 0u;
-                    for (int i = 0; i < g.KH; ++i, da_row += a_row_step) {
-                        uint64_t da = da_row;
-                        for (int j = 0; j < g.KW; ++j, da += static_cast<uint64_t>(CB >> 4), db += b_tap_step) {
 #pragma unroll
-                            for (int k = 0; k < CB / 32; ++k) {
-                                mma_i8_elect(d, da + 2 * k, db + 2 * k, idesc, acc);
-                                acc = 1u;
-                            }
+                    for (int i = 0; i < 3; ++i, da_row += a_row_step) {
+#pragma unroll
+                        for (int j = 0; j < 3; ++j, db += b_tap_step) {
+                            mma_chunk_elect<CB / 32>(d, da_row + static_cast<uint64_t>(j * (CB >> 4)), db, idesc, acc);
+                            acc = 1u;
                         }
                     }
                 } else {
                     const uint64_t db = bdesc0 + static_cast<uint64_t>(g.b_resident ? ka : s) * b_chunk_step;
-#pragma unroll
-                    for (int k = 0; k < CB / 32; ++k)
-                        mma_i8_elect(d, da0 + 2 * k, db + 2 * k, idesc, (ka | k) != 0 ? 1u : 0u);
+                    mma_chunk_elect<CB / 32>(d, da0, db, idesc, ka != 0 ? 1u : 0u);
                 }
                 if (AUX && ka == 0)
                     mma_i8_elect(d + static_cast<uint32_t>(g.aux_col), xadesc0 + static_cast<uint64_t>(s) * a_stage_step,
