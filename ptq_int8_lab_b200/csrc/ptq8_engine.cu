@@ -101,6 +101,7 @@ struct Step {
     int8_t* d_w = nullptr;
     float* d_factor = nullptr;
     float* d_bias = nullptr;
+    std::vector<float> h_factor, h_bias;   // host copies (tensor-core convs take them as kernel parameters)
     int8_t* d_im2col = nullptr;   // stem rows, bordered [N][OH+2][OW+2][kpad]
     CUtensorMap map_a{}, map_b{};
     // aux GEMM: this conv recomputes its residual (the stem's output) from the
@@ -515,13 +516,10 @@ void fill_table() {
 
 int cb_index(int cb) { return cb == 128 ? 2 : (cb == 64 ? 1 : 0); }
 
-// Dynamic shared memory of conv_tc_kernel for a pipeline shape (aux: + aux weights
-// [bn][32] and their dequantization constants).
+// Dynamic shared memory of conv_tc_kernel for a pipeline shape (aux: + aux weights [bn][32]).
 size_t conv_smem_bytes(int a_stage, int cb, int bn, int stages, int b_chunks, bool aux = false) {
     const size_t sb = (size_t)round_up(bn * cb, 1024);
-    const size_t fb = 8 * (size_t)round_up(bn, 32);
-    return 1024 + (size_t)stages * a_stage + (size_t)b_chunks * sb + fb +
-           (aux ? (size_t)round_up(bn * 32, 1024) + fb : 0);
+    return 1024 + (size_t)stages * a_stage + (size_t)b_chunks * sb + (aux ? (size_t)round_up(bn * 32, 1024) : 0);
 }
 
 // Keep the whole weight slab of the N tile resident when it fits next to a
@@ -562,10 +560,16 @@ int acc_cols_for(int bn) {
 }
 
 // Accumulator buffers in TMEM (512 columns) of `cols` columns each: 8 of <= 64
-// columns, 4 of 128, 2 of 256.  The epilogue has min(4, buffers) warp groups; each
-// owns every n_groups-th buffer.
+// columns, 4 of 128, 2 of 256.  The epilogue has min(4, buffers) warp groups, each
+// owning every n_groups-th buffer -- except for residual convs with N tiles of 49..64
+// channels, where all 16 epilogue warps take every tile, each warp a fixed 16-channel
+// slice (column-stationary: the slice's dequantization constants stay in registers;
+// measured faster only where the per-value work is large enough to pay for every
+// warp waiting on every tile).
 int n_acc_for(int cols) { return std::min(8, 512 / cols); }
-int n_groups_for(int cols) { return std::min(4, n_acc_for(cols)); }
+int n_groups_for(int cols, int bn, bool res) {
+    return res && bn > 48 && bn <= 64 ? 1 : std::min(4, n_acc_for(cols));
+}
 
 int finalize(ptq8_engine* e, int max_batch) {
     const Model& m = *e->model;
@@ -618,6 +622,8 @@ int finalize(ptq8_engine* e, int max_batch) {
             return PTQ8_ERR_CUDA;
         cudaMemcpy(st.d_factor, factor.data(), c.cout * 4, cudaMemcpyHostToDevice);
         cudaMemcpy(st.d_bias, cq.bias.data(), c.cout * 4, cudaMemcpyHostToDevice);
+        st.h_factor = factor;
+        st.h_bias = cq.bias;
         const int K = c.cin * c.kh * c.kw;
         if (st.kind == K_DW) {
             std::vector<int8_t> w((size_t)c.kh * c.kw * c.cout);
@@ -658,6 +664,8 @@ int finalize(ptq8_engine* e, int max_batch) {
         }
         st.cb = choose_cb(cpad);
         choose_bn(c.cout, &st.bn, &st.n_ntiles);
+        if (round_up(c.cout, 32) > kMaxConstCh)
+            return e->fail(strf("conv[%d]: %d output channels exceed the kernel's %d", st.conv, c.cout, kMaxConstCh));
         if (st.n_ntiles > 1 && st.bn % 32 != 0)
             return e->fail(strf("conv[%d]: N tile %d breaks the 32-byte store alignment", st.conv, st.bn));
         if (!e->dalloc(&st.d_w, w.size(), "alloc weights")) return PTQ8_ERR_CUDA;
@@ -895,14 +903,12 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.BN = st.bn;
     g.acc_cols = st.acc_cols;
     g.n_acc = n_acc_for(st.acc_cols);
-    g.n_groups = n_groups_for(st.acc_cols);
+    g.n_groups = n_groups_for(st.acc_cols, st.bn, st.res_val >= 0);
     if (st.aux_src >= 0) {
         const Step& src = e->steps[st.aux_src];
         g.aux_off = st.aux_off;
         g.aux_bytes = 128 * 32;
         g.aux_col = acc_cols_for(st.bn);
-        ep.aux_factor = src.d_factor;
-        ep.aux_bias = src.d_bias;
         ep.aux_act = src.act;
     }
     g.stages = st.stages;
@@ -910,7 +916,15 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.b_bytes = (uint32_t)(st.bn * st.cb);
     dim3 grid((unsigned)std::min(g.m_tiles, st.grid_x), (unsigned)st.n_ntiles);
     CUtensorMap ma = st.map_a, mb = st.map_b, mxa = st.map_xa, mxb = st.map_xb;
-    void* args[6] = {&ma, &mb, &mxa, &mxb, &g, &ep};
+    std::unique_ptr<ConvConsts> cc(new ConvConsts());   // zero past cout
+    std::copy(st.h_factor.begin(), st.h_factor.end(), cc->factor);
+    std::copy(st.h_bias.begin(), st.h_bias.end(), cc->bias);
+    if (st.aux_src >= 0) {
+        const Step& src = e->steps[st.aux_src];
+        std::copy(src.h_factor.begin(), src.h_factor.end(), cc->aux_factor);
+        std::copy(src.h_bias.begin(), src.h_bias.end(), cc->aux_bias);
+    }
+    void* args[7] = {&ma, &mb, &mxa, &mxb, &g, &ep, cc.get()};
     cudaLaunchKernel(st.kfn, grid, dim3(kConvThreads), args, st.smem, s);
 }
 

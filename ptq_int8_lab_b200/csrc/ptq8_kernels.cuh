@@ -481,9 +481,7 @@ struct EpiParams {
     int cout;
     int vec32;  // 1 when cout % 8 == 0: tiled fp32 maps, 256-bit loads/stores of 8 channels
     int act;    // activation of the conv itself: 0 none / 1 relu / 2 relu6
-    const float* aux_factor;   // AUX: dequantization of the aux accumulator (the residual)
-    const float* aux_bias;
-    int aux_act;
+    int aux_act;   // AUX: activation of the recomputed residual (its constants are in ConvConsts)
     int post;   // residual: 0 none, 1 add then relu, 2 add only
     // positional decomposition: channel c' = pos*dcr_oc + c of a 1x1 GEMM output is code
     // (pos / dcr_w, pos % dcr_w, c) of a dcr_h x dcr_w map (DepthToSpace, DCR order)
@@ -506,6 +504,20 @@ __device__ __forceinline__ F32At f32_at(const EpiParams& e, size_t pf, int c) {
     return {pf, c, e.cout};
 }
 
+// Per-channel dequantization constants of one tensor-core conv, passed as a
+// __grid_constant__ kernel parameter: the epilogue reads them through the
+// constant cache with warp-uniform addresses.  (Kept in shared memory, these
+// broadcast reads took over 40% of the shared-memory pipe that feeds the tensor
+// core and slowed the MMAs of the 64-channel convs by a third.)
+constexpr int kMaxConstCh = 1536;   // output channels of one conv
+constexpr int kMaxAuxCh = 256;      // output channels of an aux GEMM
+struct ConvConsts {
+    float factor[kMaxConstCh];      // float(float(s_in) * w_scale[c]), zero past cout
+    float bias[kMaxConstCh];
+    float aux_factor[kMaxAuxCh];    // AUX: the recomputed residual's constants
+    float aux_bias[kMaxAuxCh];
+};
+
 // Residual of 16 consecutive channels [c0, c0+16) of fp32 row pf (nv valid).
 __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0, int nv, float (&r)[16]) {
     const F32At a = f32_at(e, pf, c0);
@@ -518,8 +530,9 @@ __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0
     }
 }
 
-// Dequantize 16 accumulators of channels [c, c+16) (factor/bias from shared
-// memory): y = act(fadd(fmul(float(acc), factor), bias)), two roundings.
+// Dequantize 16 accumulators of channels [c, c+16) (factor/bias: 16 constants
+// each, from the kernel parameters): y = act(fadd(fmul(float(acc), factor), bias)),
+// two roundings.
 //
 // float(acc): acc + 0x4B400000 is the bit pattern of 1.5*2^23 + acc when
 // |acc| < 2^22 (exact subtraction afterwards); in that range the pattern xor
@@ -546,11 +559,10 @@ __device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float* 
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] = __int2float_rn(static_cast<int>(v[j]));
     }
-    const float4* f4 = reinterpret_cast<const float4*>(sf);
-    const float4* b4 = reinterpret_cast<const float4*>(sb);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const float4 f = f4[j], bb = b4[j];
+        const float4 f = make_float4(sf[4 * j], sf[4 * j + 1], sf[4 * j + 2], sf[4 * j + 3]);
+        const float4 bb = make_float4(sb[4 * j], sb[4 * j + 1], sb[4 * j + 2], sb[4 * j + 3]);
         y[4 * j] = __fadd_rn(__fmul_rn(y[4 * j], f.x), bb.x);
         y[4 * j + 1] = __fadd_rn(__fmul_rn(y[4 * j + 1], f.y), bb.y);
         y[4 * j + 2] = __fadd_rn(__fmul_rn(y[4 * j + 2], f.z), bb.z);
@@ -659,7 +671,7 @@ template <int CB, int MODE, int NOUT, bool RES, bool F32, bool AUX>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const __grid_constant__ CUtensorMap map_xa, const __grid_constant__ CUtensorMap map_xb,
-               const ConvGeom g, const EpiParams e) {
+               const ConvGeom g, const EpiParams e, const __grid_constant__ ConvConsts cc) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_abort;
     __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 18];  // a_full, a_empty, b_full, acc_full[8], acc_empty[8], done
@@ -677,11 +689,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     uint8_t* sA = smem;
     uint8_t* sB = smem + S * g.a_stage;
     uint8_t* sBx = sB + (g.b_resident ? g.n_kchunks : S) * sb_stride;   // aux weights [BN][32] (AUX)
-    const int sbx_bytes = AUX ? (BN * 32 + 1023) & ~1023 : 0;
-    float* s_factor = reinterpret_cast<float*>(sBx + sbx_bytes);
-    float* s_bias = s_factor + bn32;
-    float* s_afactor = s_bias + bn32;   // AUX
-    float* s_abias = s_afactor + bn32;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -718,18 +725,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     if (warp == 1) {
         tmem_alloc(smem_u32(&tslot), NA * g.acc_cols);
         tmem_relinquish();
-    }
-    if (warp >= 2) {
-        for (int c = threadIdx.x - 64; c < bn32; c += 32 * kEpiWarps) {
-            const int gc = nt * BN + c;
-            const bool ok = c < BN && gc < e.cout;
-            s_factor[c] = ok ? e.factor[gc] : 0.0f;
-            s_bias[c] = ok ? e.bias[gc] : 0.0f;
-            if (AUX) {
-                s_afactor[c] = ok ? e.aux_factor[gc] : 0.0f;
-                s_abias[c] = ok ? e.aux_bias[gc] : 0.0f;
-            }
-        }
     }
     tc_fence_before();
     __syncthreads();
@@ -882,13 +877,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         constexpr int n_out = NOUT;
         // codes can only saturate low when the values are not already clipped at zero
         const bool lower = RES ? e.post != 1 : e.act == 0;
-        int t = gi;
-        for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NG * gridDim.x, t += NG) {
-            const int buf = t % NA;
-            const uint32_t use = static_cast<uint32_t>(t / NA);
-            int n, h, w;
-            bool valid;
-            size_t pq;
+        // output position of this thread's row r in M tile mt: image n, row h, column w,
+        // bordered code row pq, fp32 row pf
+        auto position = [&](int mt, int& n, int& h, int& w, bool& valid, size_t& pq, size_t& pf) {
             if (MODE == 1) {
                 const size_t q = static_cast<size_t>(mt) * 128 + r;
                 const size_t img = static_cast<size_t>(g.Hp) * g.Wp;
@@ -907,7 +898,84 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 valid = in_tile && n < g.N && h < g.OH && w < g.OW;
                 pq = (static_cast<size_t>(n) * (g.OH + 2) + h + 1) * (g.OW + 2) + w + 1;
             }
-            const size_t pf = (static_cast<size_t>(n) * g.OH + h) * g.OW + w;
+            pf = (static_cast<size_t>(n) * g.OH + h) * g.OW + w;
+        };
+        if (NG == 1) {
+            // Column-stationary epilogue (N tile of 49..64 channels, one group): warp
+            // (quad, k) owns channels [16k, 16k+16) of its 32 rows in every tile, so its
+            // dequantization constants stay in registers for the whole kernel.
+            const int k = ew >> 2;
+            const int ch = nt * BN + k * 16;
+            const bool active = ch < tile_end;   // warp-uniform
+            const int nv = min(16, tile_end - ch);
+            float fac[16], bia[16], afac[16], abia[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                fac[j] = cc.factor[ch + j];
+                bia[j] = cc.bias[ch + j];
+                if (AUX) {
+                    afac[j] = cc.aux_factor[ch + j];
+                    abia[j] = cc.aux_bias[ch + j];
+                }
+            }
+            int t = 0;
+            for (int mt = blockIdx.x; mt < g.m_tiles; mt += gridDim.x, ++t) {
+                const int buf = t % NA;
+                const uint32_t use = static_cast<uint32_t>(t / NA);
+                int n, h, w;
+                bool valid;
+                size_t pq, pf;
+                position(mt, n, h, w, valid, pq, pf);
+                float res[16];
+                if (RES && !AUX && valid && active) load_res16(e, pf, ch, nv, res);
+                if (!mbar_wait(accf0 + 8 * buf, use & 1u)) {
+                    atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
+                    break;
+                }
+                tc_fence_after();
+                if (active) {
+                    const uint32_t trow =
+                        tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16);
+                    uint32_t v[16], vx[16];
+                    tmem_ld16(trow + k * 16, v);
+                    if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + k * 16, vx);
+                    tmem_wait_ld();
+                    if (valid) {
+                        float y[16];
+                        dequant16(v, fac, bia, e.act, y);
+                        if (AUX) dequant16(vx, afac, abia, e.aux_act, res);
+                        finish16<RES, F32>(e, pf, ch, nv, y, res);
+#pragma unroll
+                        for (int o = 0; o < 2; ++o) {
+                            if (o >= n_out) continue;
+                            int8_t* qp = code_ptr(e, o, pq, n, ch);
+                            if (nv == 16) {
+                                uint32_t w4[4];
+                                quant16q(y, o == 0 ? e.q0 : e.q1, o == 0 ? e.s0 : e.s1, lower, w4);
+                                *reinterpret_cast<uint4*>(qp) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                            } else {
+                                const float inv = o == 0 ? e.inv0 : e.inv1;
+                                const double s = o == 0 ? e.s0 : e.s1;
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    if (j < nv) qp[j] = sat8(quant_code(y[j], inv, s));
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_relaxed(acce0 + 8 * buf);
+            }
+        } else {
+        int t = gi;
+        for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NG * gridDim.x, t += NG) {
+            const int buf = t % NA;
+            const uint32_t use = static_cast<uint32_t>(t / NA);
+            int n, h, w;
+            bool valid;
+            size_t pq, pf;
+            position(mt, n, h, w, valid, pq, pf);
             // the residual does not depend on the MMAs: fetch the first half before waiting
             float res[16];
             {
@@ -936,8 +1004,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const int nv = min(16, tile_end - ch);
                     if (!valid || nv <= 0) continue;
                     float y[16];
-                    dequant16(v, s_factor + cg * 32 + hh * 16, s_bias + cg * 32 + hh * 16, e.act, y);
-                    if (AUX) dequant16(vx, s_afactor + cg * 32 + hh * 16, s_abias + cg * 32 + hh * 16, e.aux_act, res);
+                    dequant16(v, cc.factor + ch, cc.bias + ch, e.act, y);
+                    if (AUX) dequant16(vx, cc.aux_factor + ch, cc.aux_bias + ch, e.aux_act, res);
                     finish16<RES, F32>(e, pf, ch, nv, y, res);
                     // prefetch the next residual half of this warp
                     {
@@ -973,6 +1041,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_relaxed(acce0 + 8 * buf);
+        }
         }
     }
     tc_fence_before();
