@@ -53,16 +53,30 @@ def dist_env():
     return rank, world, local
 
 
-def model_files(cache: str, rank: int, world: int, barrier):
+def model_files(cache: str, rank: int, world: int, barrier, cfg: int = 4):
+    """Calibrated model files of BASELINE config `cfg` in `cache`: rank 0 writes them when
+    missing, every rank returns after the barrier."""
     from ptq_int8_lab_b200 import modelgen as mg
     d = Path(cache)
     d.mkdir(parents=True, exist_ok=True)
     tag = "resnet18_cifar_s0"
     paths = dict(model=d / f"{tag}.ptq2.bin", calib=d / f"calib_{tag}.ptqc", plan=d / f"layer_plan_{tag}.json")
     if rank == 0 and not all(p.exists() for p in paths.values()):
-        mg.make_config(4, d)
+        mg.make_config(cfg, d)
     barrier()
     return {k: str(v) for k, v in paths.items()}
+
+
+def max_over_ranks(x: float, device) -> float:
+    """The largest x over all ranks of the process group (the whole job's time); x alone
+    when there is no group or a single rank."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 class ClockSampler:
@@ -263,10 +277,7 @@ def main():
     clk = clocks.stop(t_wall0, time.time())
     ms = ev0.elapsed_time(ev1)
     eng.sync()
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, "cuda")
     ms_per_step = ms / a.steps
     value = world * B * a.steps / (ms / 1e3)
 
@@ -312,11 +323,7 @@ def main():
         eng.forward_host_ptr(xh.data_ptr(), B, 3, 32, 32, lh.data_ptr())
     e1.record(stream)
     torch.cuda.synchronize()
-    ems = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ems], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = float(t.item())
+    ems = max_over_ranks(e0.elapsed_time(e1), "cuda")
     e2e = {"value": world * B * a.steps / (ems / 1e3), "unit": "images/s",
            "h2d_bytes_per_step": B * 3 * 32 * 32 * 4, "d2h_bytes_per_step": B * 10 * 4}
 
