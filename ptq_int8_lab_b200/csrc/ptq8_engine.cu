@@ -917,12 +917,10 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     dim3 grid((unsigned)std::min(g.m_tiles, st.grid_x), (unsigned)st.n_ntiles);
     CUtensorMap ma = st.map_a, mb = st.map_b, mxa = st.map_xa, mxb = st.map_xb;
     std::unique_ptr<ConvConsts> cc(new ConvConsts());   // zero past cout
-    std::copy(st.h_factor.begin(), st.h_factor.end(), cc->factor);
-    std::copy(st.h_bias.begin(), st.h_bias.end(), cc->bias);
+    for (size_t c = 0; c < st.h_factor.size(); ++c) cc->fb[c] = make_float2(st.h_factor[c], st.h_bias[c]);
     if (st.aux_src >= 0) {
         const Step& src = e->steps[st.aux_src];
-        std::copy(src.h_factor.begin(), src.h_factor.end(), cc->aux_factor);
-        std::copy(src.h_bias.begin(), src.h_bias.end(), cc->aux_bias);
+        for (size_t c = 0; c < src.h_factor.size(); ++c) cc->aux_fb[c] = make_float2(src.h_factor[c], src.h_bias[c]);
     }
     void* args[7] = {&ma, &mb, &mxa, &mxb, &g, &ep, cc.get()};
     cudaLaunchKernel(st.kfn, grid, dim3(kConvThreads), args, st.smem, s);

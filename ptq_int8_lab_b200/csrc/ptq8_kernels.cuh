@@ -512,10 +512,9 @@ __device__ __forceinline__ F32At f32_at(const EpiParams& e, size_t pf, int c) {
 constexpr int kMaxConstCh = 1536;   // output channels of one conv
 constexpr int kMaxAuxCh = 256;      // output channels of an aux GEMM
 struct ConvConsts {
-    float factor[kMaxConstCh];      // float(float(s_in) * w_scale[c]), zero past cout
-    float bias[kMaxConstCh];
-    float aux_factor[kMaxAuxCh];    // AUX: the recomputed residual's constants
-    float aux_bias[kMaxAuxCh];
+    float2 fb[kMaxConstCh];         // (factor, bias) of channel c: one 64-bit load;
+                                    // factor = float(float(s_in) * w_scale[c]); zero past cout
+    float2 aux_fb[kMaxAuxCh];       // AUX: the recomputed residual's constants
 };
 
 // Residual of 16 consecutive channels [c0, c0+16) of fp32 row pf (nv valid).
@@ -538,8 +537,7 @@ __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0
 // |acc| < 2^22 (exact subtraction afterwards); in that range the pattern xor
 // 0x4B000000 stays below 2^23, so one OR over the 16 patterns tells whether
 // every accumulator was in range.  Otherwise the rounding conversion is used.
-__device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float* sf, const float* sb, int act,
-                                          float (&y)[16]) {
+__device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float2* fb, int act, float (&y)[16]) {
     uint32_t range = 0;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -560,13 +558,9 @@ __device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float* 
         for (int j = 0; j < 16; ++j) y[j] = __int2float_rn(static_cast<int>(v[j]));
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float4 f = make_float4(sf[4 * j], sf[4 * j + 1], sf[4 * j + 2], sf[4 * j + 3]);
-        const float4 bb = make_float4(sb[4 * j], sb[4 * j + 1], sb[4 * j + 2], sb[4 * j + 3]);
-        y[4 * j] = __fadd_rn(__fmul_rn(y[4 * j], f.x), bb.x);
-        y[4 * j + 1] = __fadd_rn(__fmul_rn(y[4 * j + 1], f.y), bb.y);
-        y[4 * j + 2] = __fadd_rn(__fmul_rn(y[4 * j + 2], f.z), bb.z);
-        y[4 * j + 3] = __fadd_rn(__fmul_rn(y[4 * j + 3], f.w), bb.w);
+    for (int j = 0; j < 16; ++j) {
+        const float2 c = fb[j];
+        y[j] = __fadd_rn(__fmul_rn(y[j], c.x), c.y);
     }
     if (act == 1) {
 #pragma unroll
@@ -908,15 +902,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const int ch = nt * BN + k * 16;
             const bool active = ch < tile_end;   // warp-uniform
             const int nv = min(16, tile_end - ch);
-            float fac[16], bia[16], afac[16], abia[16];
+            float2 fbr[16], afbr[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                fac[j] = cc.factor[ch + j];
-                bia[j] = cc.bias[ch + j];
-                if (AUX) {
-                    afac[j] = cc.aux_factor[ch + j];
-                    abia[j] = cc.aux_bias[ch + j];
-                }
+                fbr[j] = cc.fb[ch + j];
+                if (AUX) afbr[j] = cc.aux_fb[ch + j];
             }
             int t = 0;
             for (int mt = blockIdx.x; mt < g.m_tiles; mt += gridDim.x, ++t) {
@@ -942,8 +932,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     tmem_wait_ld();
                     if (valid) {
                         float y[16];
-                        dequant16(v, fac, bia, e.act, y);
-                        if (AUX) dequant16(vx, afac, abia, e.aux_act, res);
+                        dequant16(v, fbr, e.act, y);
+                        if (AUX) dequant16(vx, afbr, e.aux_act, res);
                         finish16<RES, F32>(e, pf, ch, nv, y, res);
 #pragma unroll
                         for (int o = 0; o < 2; ++o) {
@@ -1004,8 +994,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const int nv = min(16, tile_end - ch);
                     if (!valid || nv <= 0) continue;
                     float y[16];
-                    dequant16(v, cc.factor + ch, cc.bias + ch, e.act, y);
-                    if (AUX) dequant16(vx, cc.aux_factor + ch, cc.aux_bias + ch, e.aux_act, res);
+                    dequant16(v, cc.fb + ch, e.act, y);
+                    if (AUX) dequant16(vx, cc.aux_fb + ch, e.aux_act, res);
                     finish16<RES, F32>(e, pf, ch, nv, y, res);
                     // prefetch the next residual half of this warp
                     {
