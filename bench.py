@@ -296,13 +296,14 @@ def main():
     hbm, bf16, src = measured_peaks()
     int8_peak = 2.0 * bf16   # dense int8 tensor rate is twice the dense bf16 rate on B200
     achieved = tc_ops / (tc_ms / 1e3) / 1e12
+    # DRAM bytes of all dense-conv launches of one forward, from the committed ncu summary
+    # (captured at batch 2048 and scaled by 4; see the file); per forward like `achieved`
     traffic = None
-    tp = ROOT / "profiles" / "conv_tc_traffic.json"
-    if tp.exists():
-        try:
-            traffic = json.loads(tp.read_text()).get("dram_bytes_per_forward_b8192")
-        except Exception:
-            traffic = None
+    tp = ROOT / "profiles" / "conv_tc_traffic_resnet18_b8192.txt"
+    if tp.exists() and B == 8192:
+        for line in tp.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_forward_b8192 ="):
+                traffic = int(line.split("=")[1].strip())
     roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
                 "frac": achieved / int8_peak, "traffic": traffic,
                 "kernel": "conv_tc_kernel (all dense convs of one forward)",
