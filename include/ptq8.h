@@ -160,6 +160,46 @@ int ptq8_engine_n_launches(const ptq8_engine* e);
 /* Human-readable record of what the graph passes did. */
 int ptq8_engine_passes_log(const ptq8_engine* e, char* out, size_t cap);
 
+/* ---- one-call interface ----------------------------------------------------
+ * The same engine behind five calls, for callers that do not need the steps
+ * above.  Status codes only (the reference's forward exits on CUDA errors,
+ * int8_engine.cuh:109-117); messages via ptq8_last_error. */
+
+typedef struct ptq8_opts {
+    int device;      /* CUDA device ordinal */
+    int w_bits;      /* weight bits (8 or 4) when no layer plan is given (Int8Engine::build w_bits) */
+    int a_bits;      /* activation bits: 8 */
+    int act_mode;    /* PTQ8_ACT_ABSMAX (default, ref_int8.py:69-87) or PTQ8_ACT_MINMAX */
+    int passes;      /* PTQ8_PASS_* bits: graph passes on the quantized layers */
+    int max_batch;   /* device scratch for this many images; 0: sized by the first forward */
+} ptq8_opts;
+
+/* Model::load (ptq_model.h:72) + load_ptqc (:425) + layer plan (mixed_check.py:62-81,
+ * per-layer bits 4/8, per_channel only) + Int8Engine::build / set_act_mode /
+ * set_calib / alloc_scratch (int8_engine.cuh:132,353,362,807) in one call.  PTQ2
+ * and PTQW files are accepted unchanged; plan_json may be NULL.  opts NULL means
+ * {device 0, W8, A8, AbsMax, no passes, max_batch 0}.  The engine owns the model.
+ * On failure *out is NULL and err holds the message. */
+int ptq8_load(const char* model_path, const char* calib_path, const char* plan_json, const ptq8_opts* opts,
+              ptq8_engine** out, char* err, size_t errlen);
+/* Forward of n images (fp32 NCHW at x_dev) into logits_dev [n][fc_out], both device
+ * pointers, asynchronous on `stream` (NULL: the engine's stream).  Replaces
+ * Int8Engine::forward (int8_engine.cuh:429) without its host copies. */
+int ptq8_forward(ptq8_engine* e, const float* x_dev, int n, float* logits_dev, void* stream);
+/* ptq8_forward, then (synchronously) the int8 input codes of every conv, handed to
+ * dump(user, conv, codes, n, h, w, ld) as a host array [n][h][w][ld] (the stem's
+ * are its im2col rows) -- the parity hook that replaces forward(...,
+ * stop_after_block, mid_out) and locate_block.cpp. */
+typedef void (*ptq8_dump_fn)(void* user, int conv, const int8_t* codes, int n, int h, int w, int ld);
+int ptq8_forward_debug(ptq8_engine* e, const float* x_dev, int n, float* logits_dev, void* stream,
+                       ptq8_dump_fn dump, void* user);
+/* Capture (and cache) the CUDA graph of a forward at batch n ahead of the first
+ * forward (the reference launches kernel by kernel with no graph). */
+int ptq8_capture_graph(ptq8_engine* e, int n);
+/* Destroy an engine and, when it came from ptq8_load, its model. */
+void ptq8_destroy(ptq8_engine* e);
+const char* ptq8_last_error(const ptq8_engine* e);
+
 #ifdef __cplusplus
 }
 #endif

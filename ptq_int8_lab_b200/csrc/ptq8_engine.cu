@@ -20,6 +20,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -134,6 +135,7 @@ struct ptq8_engine {
     bool own_stream = false;
     std::string err;
     const Model* model = nullptr;   // caller keeps the model alive (int8_engine.cuh:134)
+    ptq8_model* owned_model = nullptr;   // set by ptq8_load: freed with the engine
     int w_bits = 8, a_bits = 8, act_mode = ACT_ABSMAX, passes = 0;
     std::vector<int> layer_bits;
     std::vector<ConvQ> q;
@@ -963,7 +965,8 @@ void step_work(const ptq8_engine* e, int n, size_t si, double* macs, double* byt
     *bytes = inb + (double)c.cout * c.cin * c.kh * c.kw + outb + resb;
 }
 
-int launch(ptq8_engine* e, int n, bool use_graph) {
+// The CUDA graph of one forward at batch n (captured on first use, then cached).
+int graph_for(ptq8_engine* e, int n, cudaGraphExec_t* out) {
     if (!e->planned) {
         int rc = finalize(e, std::max(n, e->max_batch > 0 ? e->max_batch : n));
         if (rc) return rc;
@@ -971,7 +974,6 @@ int launch(ptq8_engine* e, int n, bool use_graph) {
     if (n <= 0 || n > e->max_batch)
         return e->fail(strf("batch %d outside [1, %d] (alloc_scratch sets the maximum)", n, e->max_batch));
     if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
-    if (!use_graph) return enqueue(e, n);
     auto it = e->graphs.find(n);
     if (it == e->graphs.end()) {
         cudaGraph_t g;
@@ -987,7 +989,25 @@ int launch(ptq8_engine* e, int n, bool use_graph) {
         if (!e->cuda_ok(ce, "graph instantiate")) return PTQ8_ERR_CUDA;
         it = e->graphs.emplace(n, ge).first;
     }
-    if (!e->cuda_ok(cudaGraphLaunch(it->second, e->stream), "graph launch")) return PTQ8_ERR_CUDA;
+    *out = it->second;
+    return PTQ8_OK;
+}
+
+int launch(ptq8_engine* e, int n, bool use_graph) {
+    if (!use_graph) {
+        if (!e->planned) {
+            int rc = finalize(e, std::max(n, e->max_batch > 0 ? e->max_batch : n));
+            if (rc) return rc;
+        }
+        if (n <= 0 || n > e->max_batch)
+            return e->fail(strf("batch %d outside [1, %d] (alloc_scratch sets the maximum)", n, e->max_batch));
+        if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
+        return enqueue(e, n);
+    }
+    cudaGraphExec_t ge;
+    int rc = graph_for(e, n, &ge);
+    if (rc) return rc;
+    if (!e->cuda_ok(cudaGraphLaunch(ge, e->stream), "graph launch")) return PTQ8_ERR_CUDA;
     return PTQ8_OK;
 }
 
@@ -1039,19 +1059,23 @@ extern "C" {
 int ptq8_abi_version(void) { return PTQ8_ABI_VERSION; }
 
 ptq8_model* ptq8_model_load(const char* path, char* err, size_t errlen) {
-    if (!path) {
-        copy_err("null path", err, errlen);
+    try {
+        if (!path) {
+            copy_err("null path", err, errlen);
+            return nullptr;
+        }
+        std::unique_ptr<ptq8_model> m(new ptq8_model());
+        std::string e;
+        if (!m->m.load(path, &e)) {
+            copy_err(e, err, errlen);
+            return nullptr;
+        }
+        copy_err("", err, errlen);
+        return m.release();
+    } catch (const std::exception& ex) {
+        copy_err(std::string("ptq8_model_load: ") + ex.what(), err, errlen);
         return nullptr;
     }
-    auto* m = new ptq8_model();
-    std::string e;
-    if (!m->m.load(path, &e)) {
-        copy_err(e, err, errlen);
-        delete m;
-        return nullptr;
-    }
-    copy_err("", err, errlen);
-    return m;
 }
 
 void ptq8_model_free(ptq8_model* m) { delete m; }
@@ -1116,28 +1140,33 @@ int ptq8_model_weights(const ptq8_model* mm, int i, const float** weight, size_t
 }
 
 int ptq8_load_ptqc(const char* path, size_t n_expected, float* lohi, size_t cap, char* err, size_t errlen) {
-    if (!path) {
-        copy_err("null path", err, errlen);
-        return PTQ8_ERR_INVALID;
-    }
-    std::vector<std::pair<float, float>> r;
-    std::string e;
-    if (!load_ptqc(path, n_expected, &r, &e)) {
-        copy_err(e, err, errlen);
-        return PTQ8_ERR_FORMAT;
-    }
-    if (lohi) {
-        if (cap < 2 * r.size()) {
-            copy_err("output buffer too small", err, errlen);
+    try {
+        if (!path) {
+            copy_err("null path", err, errlen);
             return PTQ8_ERR_INVALID;
         }
-        for (size_t k = 0; k < r.size(); ++k) {
-            lohi[2 * k] = r[k].first;
-            lohi[2 * k + 1] = r[k].second;
+        std::vector<std::pair<float, float>> r;
+        std::string e;
+        if (!load_ptqc(path, n_expected, &r, &e)) {
+            copy_err(e, err, errlen);
+            return PTQ8_ERR_FORMAT;
         }
+        if (lohi) {
+            if (cap < 2 * r.size()) {
+                copy_err("output buffer too small", err, errlen);
+                return PTQ8_ERR_INVALID;
+            }
+            for (size_t k = 0; k < r.size(); ++k) {
+                lohi[2 * k] = r[k].first;
+                lohi[2 * k + 1] = r[k].second;
+            }
+        }
+        copy_err("", err, errlen);
+        return PTQ8_OK;
+    } catch (const std::exception& ex) {
+        copy_err(std::string("ptq8_load_ptqc: ") + ex.what(), err, errlen);
+        return PTQ8_ERR_FORMAT;
     }
-    copy_err("", err, errlen);
-    return PTQ8_OK;
 }
 
 double ptq8_act_scale(float lo, float hi, int bits, int mode) { return act_scale_from_range(lo, hi, bits, mode); }
@@ -1240,69 +1269,73 @@ const char* ptq8_engine_last_error(const ptq8_engine* e) { return e ? e->err.c_s
 
 int ptq8_engine_build(ptq8_engine* e, const ptq8_model* mm, int w_bits, int a_bits, const int* layer_bits,
                       int n_layer_bits, int passes) {
-    if (!e || !mm) return PTQ8_ERR_INVALID;
-    const Model& m = mm->m;
-    if (a_bits != 8) return e->fail(strf("a_bits=%d unsupported (int8 activations only)", a_bits));
-    if (w_bits != 8 && w_bits != 4) return e->fail(strf("w_bits=%d unsupported (8 or 4)", w_bits));
-    if (layer_bits && n_layer_bits != (int)m.convs.size())
-        return e->fail(strf("layer plan has %d entries but the model has %zu convs", n_layer_bits, m.convs.size()));
-    e->model = &m;
-    e->w_bits = w_bits;
-    e->a_bits = a_bits;
-    e->passes = passes;
-    e->layer_bits.assign(m.convs.size(), w_bits);
-    if (layer_bits)
-        for (size_t i = 0; i < m.convs.size(); ++i) {
-            if (layer_bits[i] != 8 && layer_bits[i] != 4)
-                return e->fail(strf("layer plan: conv %zu bits=%d (4/8 only)", i, layer_bits[i]));
-            e->layer_bits[i] = layer_bits[i];
-        }
-    std::string verr;
-    if (!m.validate(&verr, e->in_h, e->in_w)) return e->fail(verr);
-    e->q.assign(m.convs.size(), ConvQ());
-    for (size_t i = 0; i < m.convs.size(); ++i) {
-        const ConvSpec& c = m.convs[i];
-        ConvQ& cq = e->q[i];
-        cq.spec = c;
-        cq.spec.weight.clear();
-        cq.spec.bias.clear();
-        cq.bits = e->layer_bits[i];
-        const int K = c.cin * c.kh * c.kw;
-        cq.codes.resize((size_t)c.cout * K);
-        cq.wscale.resize(c.cout);
-        quantize_weight_per_channel(c.weight.data(), c.cout, K, cq.bits, cq.codes.data(), cq.wscale.data());
-        cq.bias = c.bias;
-    }
-    // graph passes run on the quantized layers (codes + scales), so they are exact
-    if (passes) {
-        int h = conv_out_dim(e->in_h, m.convs[0].kh, m.convs[0].sh, m.convs[0].ph);
-        int w = conv_out_dim(e->in_w, m.convs[0].kw, m.convs[0].sw, m.convs[0].pw);
-        if (m.stem_pool) { h = (h + 2 - 3) / 2 + 1; w = (w + 2 - 3) / 2 + 1; }
-        for (size_t bi = 0; bi < m.blocks.size(); ++bi) {
-            const BlockSpec& b = m.blocks[bi];
-            auto try_conv = [&](int ci, int ih, int iw) {
-                std::string note;
-                bool done = false;
-                if (passes & PTQ8_PASS_CENTER_TAP) done = center_tap(e->q[ci], ih, iw, &note);
-                if (!done && (passes & PTQ8_PASS_DECOMPOSE)) done = decompose(e->q[ci], ih, iw, &note);
-                e->passes_log.push_back(strf("conv[%d] in %dx%d: %s", ci, ih, iw, done ? note.c_str() : "unchanged"));
-            };
-            if (b.ds >= 0) try_conv(b.ds, h, w);
-            int th = h, tw = w;
-            for (int ci : b.convs) {
-                if (ci < 0) continue;
-                const ConvSpec& c = m.convs[ci];
-                try_conv(ci, th, tw);
-                th = conv_out_dim(th, c.kh, c.sh, c.ph);
-                tw = conv_out_dim(tw, c.kw, c.sw, c.pw);
+    try {
+        if (!e || !mm) return PTQ8_ERR_INVALID;
+        const Model& m = mm->m;
+        if (a_bits != 8) return e->fail(strf("a_bits=%d unsupported (int8 activations only)", a_bits));
+        if (w_bits != 8 && w_bits != 4) return e->fail(strf("w_bits=%d unsupported (8 or 4)", w_bits));
+        if (layer_bits && n_layer_bits != (int)m.convs.size())
+            return e->fail(strf("layer plan has %d entries but the model has %zu convs", n_layer_bits, m.convs.size()));
+        e->model = &m;
+        e->w_bits = w_bits;
+        e->a_bits = a_bits;
+        e->passes = passes;
+        e->layer_bits.assign(m.convs.size(), w_bits);
+        if (layer_bits)
+            for (size_t i = 0; i < m.convs.size(); ++i) {
+                if (layer_bits[i] != 8 && layer_bits[i] != 4)
+                    return e->fail(strf("layer plan: conv %zu bits=%d (4/8 only)", i, layer_bits[i]));
+                e->layer_bits[i] = layer_bits[i];
             }
-            h = th;
-            w = tw;
+        std::string verr;
+        if (!m.validate(&verr, e->in_h, e->in_w)) return e->fail(verr);
+        e->q.assign(m.convs.size(), ConvQ());
+        for (size_t i = 0; i < m.convs.size(); ++i) {
+            const ConvSpec& c = m.convs[i];
+            ConvQ& cq = e->q[i];
+            cq.spec = c;
+            cq.spec.weight.clear();
+            cq.spec.bias.clear();
+            cq.bits = e->layer_bits[i];
+            const int K = c.cin * c.kh * c.kw;
+            cq.codes.resize((size_t)c.cout * K);
+            cq.wscale.resize(c.cout);
+            quantize_weight_per_channel(c.weight.data(), c.cout, K, cq.bits, cq.codes.data(), cq.wscale.data());
+            cq.bias = c.bias;
         }
+        // graph passes run on the quantized layers (codes + scales), so they are exact
+        if (passes) {
+            int h = conv_out_dim(e->in_h, m.convs[0].kh, m.convs[0].sh, m.convs[0].ph);
+            int w = conv_out_dim(e->in_w, m.convs[0].kw, m.convs[0].sw, m.convs[0].pw);
+            if (m.stem_pool) { h = (h + 2 - 3) / 2 + 1; w = (w + 2 - 3) / 2 + 1; }
+            for (size_t bi = 0; bi < m.blocks.size(); ++bi) {
+                const BlockSpec& b = m.blocks[bi];
+                auto try_conv = [&](int ci, int ih, int iw) {
+                    std::string note;
+                    bool done = false;
+                    if (passes & PTQ8_PASS_CENTER_TAP) done = center_tap(e->q[ci], ih, iw, &note);
+                    if (!done && (passes & PTQ8_PASS_DECOMPOSE)) done = decompose(e->q[ci], ih, iw, &note);
+                    e->passes_log.push_back(strf("conv[%d] in %dx%d: %s", ci, ih, iw, done ? note.c_str() : "unchanged"));
+                };
+                if (b.ds >= 0) try_conv(b.ds, h, w);
+                int th = h, tw = w;
+                for (int ci : b.convs) {
+                    if (ci < 0) continue;
+                    const ConvSpec& c = m.convs[ci];
+                    try_conv(ci, th, tw);
+                    th = conv_out_dim(th, c.kh, c.sh, c.ph);
+                    tw = conv_out_dim(tw, c.kw, c.sw, c.pw);
+                }
+                h = th;
+                w = tw;
+            }
+        }
+        e->built = true;
+        e->planned = false;
+        return PTQ8_OK;
+    } catch (const std::exception& ex) {
+        return e->fail(std::string("build: ") + ex.what());
     }
-    e->built = true;
-    e->planned = false;
-    return PTQ8_OK;
 }
 
 int ptq8_engine_set_act_mode(ptq8_engine* e, int mode) {
@@ -1467,48 +1500,52 @@ int ptq8_engine_tensor_info(ptq8_engine* e, int what, int index, int* shape4) {
 }
 
 int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst, size_t bytes) {
-    if (!e || !e->planned || !host_dst || n <= 0 || n > e->max_batch) return PTQ8_ERR_INVALID;
-    int shp[4];
-    int rc = ptq8_engine_tensor_info(e, what, index, shp);
-    if (rc) return rc;
-    const size_t elem = what == 0 ? 1 : sizeof(float);
-    const size_t need = (size_t)n * shp[1] * shp[2] * shp[3] * elem;
-    if (bytes < need) return e->fail("dump buffer too small");
-    if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "sync")) return PTQ8_ERR_CUDA;
-    if (what == 0) {
-        const Step& st = e->steps[e->conv_step[index]];
-        if (st.kind == K_STEM_IM2COL) {   // drop the border rows of the bordered im2col map
-            const size_t row = (size_t)st.ow * st.kpad, prow = (size_t)(st.ow + 2) * st.kpad;
+    try {
+        if (!e || !e->planned || !host_dst || n <= 0 || n > e->max_batch) return PTQ8_ERR_INVALID;
+        int shp[4];
+        int rc = ptq8_engine_tensor_info(e, what, index, shp);
+        if (rc) return rc;
+        const size_t elem = what == 0 ? 1 : sizeof(float);
+        const size_t need = (size_t)n * shp[1] * shp[2] * shp[3] * elem;
+        if (bytes < need) return e->fail("dump buffer too small");
+        if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "sync")) return PTQ8_ERR_CUDA;
+        if (what == 0) {
+            const Step& st = e->steps[e->conv_step[index]];
+            if (st.kind == K_STEM_IM2COL) {   // drop the border rows of the bordered im2col map
+                const size_t row = (size_t)st.ow * st.kpad, prow = (size_t)(st.ow + 2) * st.kpad;
+                for (int i = 0; i < n; ++i) {
+                    const int8_t* s0 = st.d_im2col + ((size_t)i * (st.oh + 2) + 1) * prow + st.kpad;
+                    int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * st.oh * row;
+                    if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, st.oh, cudaMemcpyDeviceToHost), "dump"))
+                        return PTQ8_ERR_CUDA;
+                }
+                return PTQ8_OK;
+            }
+            const Value& v = e->vals[st.in_val];
+            const int8_t* src = v.codes[v.code_index(st.s_in)];
+            // drop the one-pixel border: per image, H rows of W*ld bytes out of (H+2) x (W+2)*ld
+            const size_t row = (size_t)v.w * v.ldq, prow = (size_t)(v.w + 2) * v.ldq;
             for (int i = 0; i < n; ++i) {
-                const int8_t* s0 = st.d_im2col + ((size_t)i * (st.oh + 2) + 1) * prow + st.kpad;
-                int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * st.oh * row;
-                if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, st.oh, cudaMemcpyDeviceToHost), "dump"))
+                const int8_t* s0 = src + ((size_t)i * (v.h + 2) + 1) * prow + v.ldq;
+                int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * v.h * row;
+                if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, v.h, cudaMemcpyDeviceToHost), "dump"))
                     return PTQ8_ERR_CUDA;
             }
             return PTQ8_OK;
         }
-        const Value& v = e->vals[st.in_val];
-        const int8_t* src = v.codes[v.code_index(st.s_in)];
-        // drop the one-pixel border: per image, H rows of W*ld bytes out of (H+2) x (W+2)*ld
-        const size_t row = (size_t)v.w * v.ldq, prow = (size_t)(v.w + 2) * v.ldq;
-        for (int i = 0; i < n; ++i) {
-            const int8_t* s0 = src + ((size_t)i * (v.h + 2) + 1) * prow + v.ldq;
-            int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * v.h * row;
-            if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, v.h, cudaMemcpyDeviceToHost), "dump"))
-                return PTQ8_ERR_CUDA;
-        }
+        // the device map is in the f32_off layout: copy whole blocks, then reorder to NHWC
+        const Value& fv = e->vals[e->final_val];
+        const size_t npos = (size_t)n * shp[1] * shp[2];
+        std::vector<float> raw(((npos + 31) & ~(size_t)31) * fv.c);
+        if (!e->cuda_ok(cudaMemcpy(raw.data(), fv.f32, raw.size() * sizeof(float), cudaMemcpyDeviceToHost), "dump"))
+            return PTQ8_ERR_CUDA;
+        float* dst = static_cast<float*>(host_dst);
+        for (size_t p = 0; p < npos; ++p)
+            for (int c = 0; c < fv.c; ++c) dst[p * fv.c + c] = raw[f32_off(p, c, fv.c)];
         return PTQ8_OK;
+    } catch (const std::exception& ex) {
+        return e->fail(std::string("dump: ") + ex.what());
     }
-    // the device map is in the f32_off layout: copy whole blocks, then reorder to NHWC
-    const Value& fv = e->vals[e->final_val];
-    const size_t npos = (size_t)n * shp[1] * shp[2];
-    std::vector<float> raw(((npos + 31) & ~(size_t)31) * fv.c);
-    if (!e->cuda_ok(cudaMemcpy(raw.data(), fv.f32, raw.size() * sizeof(float), cudaMemcpyDeviceToHost), "dump"))
-        return PTQ8_ERR_CUDA;
-    float* dst = static_cast<float*>(host_dst);
-    for (size_t p = 0; p < npos; ++p)
-        for (int c = 0; c < fv.c; ++c) dst[p * fv.c + c] = raw[f32_off(p, c, fv.c)];
-    return PTQ8_OK;
 }
 
 int ptq8_engine_profile(ptq8_engine* e, int n, int iters, float* ms, double* macs, double* bytes, int* kind,
@@ -1564,5 +1601,99 @@ int ptq8_engine_passes_log(const ptq8_engine* e, char* out, size_t cap) {
     std::snprintf(out, cap, "%s", s.c_str());
     return PTQ8_OK;
 }
+
+// ---- one-call interface (load / forward / debug / capture / destroy)
+
+int ptq8_load(const char* model_path, const char* calib_path, const char* plan_json, const ptq8_opts* opts,
+              ptq8_engine** out, char* err, size_t errlen) {
+    try {
+        if (out) *out = nullptr;
+        if (!model_path || !calib_path || !out) {
+            copy_err("null model path, calibration path or output pointer", err, errlen);
+            return PTQ8_ERR_INVALID;
+        }
+        const ptq8_opts o = opts ? *opts : ptq8_opts{0, 8, 8, PTQ8_ACT_ABSMAX, 0, 0};
+        ptq8_model* m = ptq8_model_load(model_path, err, errlen);
+        if (!m) return PTQ8_ERR_FORMAT;
+        const size_t nconv = m->m.convs.size();
+        std::vector<float> lohi(2 * nconv);
+        int rc = ptq8_load_ptqc(calib_path, nconv, lohi.data(), lohi.size(), err, errlen);
+        if (rc) {
+            ptq8_model_free(m);
+            return rc;
+        }
+        std::vector<int> bits;
+        std::string why;
+        if (plan_json && !load_layer_plan(plan_json, nconv, &bits, &why)) {
+            copy_err(why, err, errlen);
+            ptq8_model_free(m);
+            return PTQ8_ERR_FORMAT;
+        }
+        ptq8_engine* e = ptq8_engine_create(o.device);
+        e->owned_model = m;
+        rc = ptq8_engine_build(e, m, o.w_bits, o.a_bits, bits.empty() ? nullptr : bits.data(), (int)bits.size(),
+                               o.passes);
+        if (!rc) rc = ptq8_engine_set_act_mode(e, o.act_mode);
+        if (!rc) rc = ptq8_engine_set_calib(e, lohi.data(), nconv);
+        if (!rc && o.max_batch > 0) rc = ptq8_engine_alloc_scratch(e, o.max_batch);
+        if (rc) {
+            copy_err(e->err.empty() ? std::string("engine set-up failed") : e->err, err, errlen);
+            ptq8_destroy(e);
+            return rc;
+        }
+        copy_err("", err, errlen);
+        *out = e;
+        return PTQ8_OK;
+    } catch (const std::exception& ex) {
+        copy_err(std::string("ptq8_load: ") + ex.what(), err, errlen);
+        return PTQ8_ERR_INVALID;
+    }
+}
+
+int ptq8_forward(ptq8_engine* e, const float* x_dev, int n, float* logits_dev, void* stream) {
+    if (!e) return PTQ8_ERR_INVALID;
+    if (stream && static_cast<cudaStream_t>(stream) != e->stream) {
+        const int rc = ptq8_engine_set_stream(e, stream);
+        if (rc) return rc;
+    }
+    return ptq8_engine_forward_device(e, x_dev, n, logits_dev);
+}
+
+int ptq8_forward_debug(ptq8_engine* e, const float* x_dev, int n, float* logits_dev, void* stream,
+                       ptq8_dump_fn dump, void* user) {
+    try {
+        if (!e || !dump) return PTQ8_ERR_INVALID;
+        int rc = ptq8_forward(e, x_dev, n, logits_dev, stream);
+        if (rc) return rc;
+        if ((rc = ptq8_engine_sync(e)) != 0) return rc;
+        std::vector<int8_t> buf;
+        for (int i = 0; i < (int)e->conv_step.size(); ++i) {
+            if (e->conv_step[i] < 0) continue;   // conv folded away by a graph pass
+            int shp[4];
+            if ((rc = ptq8_engine_tensor_info(e, 0, i, shp)) != 0) return rc;
+            buf.resize((size_t)n * shp[1] * shp[2] * shp[3]);
+            if ((rc = ptq8_engine_dump(e, 0, i, n, buf.data(), buf.size())) != 0) return rc;
+            dump(user, i, buf.data(), n, shp[1], shp[2], shp[3]);
+        }
+        return PTQ8_OK;
+    } catch (const std::exception& ex) {
+        return e->fail(std::string("forward_debug: ") + ex.what());
+    }
+}
+
+int ptq8_capture_graph(ptq8_engine* e, int n) {
+    if (!e) return PTQ8_ERR_INVALID;
+    cudaGraphExec_t ge;
+    return graph_for(e, n, &ge);
+}
+
+void ptq8_destroy(ptq8_engine* e) {
+    if (!e) return;
+    ptq8_model* m = e->owned_model;
+    ptq8_engine_destroy(e);
+    ptq8_model_free(m);   // after the engine, which points into it
+}
+
+const char* ptq8_last_error(const ptq8_engine* e) { return ptq8_engine_last_error(e); }
 
 }  // extern "C"

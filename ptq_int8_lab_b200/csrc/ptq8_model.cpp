@@ -6,7 +6,10 @@
 #include <cstdio>
 #include <cstring>
 #include <fstream>
+#include <sys/stat.h>
+#include <iterator>
 #include <limits>
+#include <string>
 
 namespace ptq8 {
 
@@ -26,15 +29,21 @@ bool fail(std::string* err, const std::string& m) {
     return false;
 }
 
+constexpr uint64_t kMaxFileBytes = 1ull << 32;
+
 // Bounds-checked little-endian reader over a whole file held in memory.
 class Reader {
 public:
     bool open(const std::string& path, std::string* err) {
+        struct stat st {};
+        if (::stat(path.c_str(), &st) != 0) return fail(err, "cannot open file: " + path);
+        if (!S_ISREG(st.st_mode)) return fail(err, "not a regular file: " + path);
+        if (st.st_size > (off_t)kMaxFileBytes) return fail(err, "file larger than 4 GiB: " + path);
         std::ifstream f(path, std::ios::binary);
         if (!f.is_open()) return fail(err, "cannot open file: " + path);
         f.seekg(0, std::ios::end);
         std::streamoff end = f.tellg();
-        if (!f || end < 0) return fail(err, "cannot read file size: " + path);
+        if (!f || end < 0 || end > (std::streamoff)kMaxFileBytes) return fail(err, "cannot read file size: " + path);
         buf_.resize((size_t)end);
         f.seekg(0, std::ios::beg);
         if (end > 0) f.read(reinterpret_cast<char*>(buf_.data()), end);
@@ -358,6 +367,187 @@ void quantize_weight_per_channel(const float* w, int cout, int k, int bits, int8
             codes[(size_t)o * k + i] = (int8_t)v;
         }
     }
+}
+
+
+// ---------------------------------------------------------------- layer plan JSON
+
+namespace {
+
+// A small strict JSON reader (RFC 8259 values; strings without \u escapes
+// beyond the ASCII range), enough for the layer-plan files.
+struct JValue {
+    enum Kind { NUL, BOOL, NUM, STR, ARR, OBJ } kind = NUL;
+    bool b = false;
+    double num = 0.0;
+    std::string str;
+    std::vector<JValue> arr;
+    std::vector<std::pair<std::string, JValue>> obj;
+    const JValue* get(const char* key) const {
+        for (const auto& kv : obj)
+            if (kv.first == key) return &kv.second;
+        return nullptr;
+    }
+};
+
+struct JParser {
+    const std::string& t;
+    size_t i = 0;
+    std::string err;
+    explicit JParser(const std::string& text) : t(text) {}
+    void ws() {
+        while (i < t.size() && (t[i] == ' ' || t[i] == '\n' || t[i] == '\r' || t[i] == '\t')) ++i;
+    }
+    bool fail(const char* what) {
+        if (err.empty()) err = fmt("JSON: %s at byte %zu", what, i);
+        return false;
+    }
+    bool lit(const char* w) {
+        const size_t n = std::strlen(w);
+        if (t.compare(i, n, w) != 0) return fail("bad literal");
+        i += n;
+        return true;
+    }
+    bool string(std::string* out) {
+        if (t[i] != '"') return fail("expected string");
+        ++i;
+        out->clear();
+        while (i < t.size() && t[i] != '"') {
+            char c = t[i++];
+            if (c == '\\') {
+                if (i >= t.size()) return fail("bad escape");
+                const char e = t[i++];
+                switch (e) {
+                    case '"': case '\\': case '/': c = e; break;
+                    case 'b': c = '\b'; break;
+                    case 'f': c = '\f'; break;
+                    case 'n': c = '\n'; break;
+                    case 'r': c = '\r'; break;
+                    case 't': c = '\t'; break;
+                    case 'u': {
+                        if (i + 4 > t.size()) return fail("bad \\u escape");
+                        const unsigned v = static_cast<unsigned>(std::strtoul(t.substr(i, 4).c_str(), nullptr, 16));
+                        i += 4;
+                        if (v > 0x7f) return fail("non-ASCII \\u escape");
+                        c = static_cast<char>(v);
+                        break;
+                    }
+                    default: return fail("bad escape");
+                }
+            }
+            out->push_back(c);
+        }
+        if (i >= t.size()) return fail("unterminated string");
+        ++i;
+        return true;
+    }
+    bool value(JValue* v, int depth) {
+        if (depth > 64) return fail("nesting too deep");
+        ws();
+        if (i >= t.size()) return fail("unexpected end");
+        const char c = t[i];
+        if (c == '{') {
+            v->kind = JValue::OBJ;
+            ++i;
+            ws();
+            if (i < t.size() && t[i] == '}') { ++i; return true; }
+            while (true) {
+                ws();
+                std::string key;
+                if (i >= t.size() || !string(&key)) return fail("expected key");
+                ws();
+                if (i >= t.size() || t[i] != ':') return fail("expected ':'");
+                ++i;
+                v->obj.emplace_back(key, JValue());
+                if (!value(&v->obj.back().second, depth + 1)) return false;
+                ws();
+                if (i < t.size() && t[i] == ',') { ++i; continue; }
+                if (i < t.size() && t[i] == '}') { ++i; return true; }
+                return fail("expected ',' or '}'");
+            }
+        }
+        if (c == '[') {
+            v->kind = JValue::ARR;
+            ++i;
+            ws();
+            if (i < t.size() && t[i] == ']') { ++i; return true; }
+            while (true) {
+                v->arr.emplace_back();
+                if (!value(&v->arr.back(), depth + 1)) return false;
+                ws();
+                if (i < t.size() && t[i] == ',') { ++i; continue; }
+                if (i < t.size() && t[i] == ']') { ++i; return true; }
+                return fail("expected ',' or ']'");
+            }
+        }
+        if (c == '"') {
+            v->kind = JValue::STR;
+            return string(&v->str);
+        }
+        if (c == 't') { v->kind = JValue::BOOL; v->b = true; return lit("true"); }
+        if (c == 'f') { v->kind = JValue::BOOL; v->b = false; return lit("false"); }
+        if (c == 'n') { v->kind = JValue::NUL; return lit("null"); }
+        if (c == '-' || (c >= '0' && c <= '9')) {
+            const char* s0 = t.c_str() + i;
+            char* end = nullptr;
+            v->kind = JValue::NUM;
+            v->num = std::strtod(s0, &end);
+            if (end == s0) return fail("bad number");
+            i += static_cast<size_t>(end - s0);
+            return true;
+        }
+        return fail("unexpected character");
+    }
+};
+
+}  // namespace
+
+bool load_layer_plan(const std::string& path, size_t n_conv, std::vector<int>* bits, std::string* err) {
+    struct stat st {};
+    if (::stat(path.c_str(), &st) != 0 || !S_ISREG(st.st_mode) || st.st_size > (off_t)(64u << 20)) {
+        *err = "cannot open layer plan (not a regular file of at most 64 MiB): " + path;
+        return false;
+    }
+    std::ifstream f(path, std::ios::binary);
+    if (!f) {
+        *err = "cannot open " + path;
+        return false;
+    }
+    std::string text((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+    JParser p(text);
+    JValue doc;
+    if (!p.value(&doc, 0)) {
+        *err = path + ": " + p.err;
+        return false;
+    }
+    p.ws();
+    if (p.i != text.size()) {
+        *err = path + ": trailing data after the JSON document";
+        return false;
+    }
+    const JValue* layers = doc.kind == JValue::OBJ ? doc.get("layers") : nullptr;
+    if (!layers || layers->kind != JValue::ARR || layers->arr.size() != n_conv) {
+        *err = fmt("%s: 'layers' must list %zu convs in engine order", path.c_str(), n_conv);
+        return false;
+    }
+    bits->clear();
+    for (size_t k = 0; k < n_conv; ++k) {
+        const JValue& e = layers->arr[k];
+        const JValue* b = e.kind == JValue::OBJ ? e.get("bits") : nullptr;
+        const int v = b && b->kind == JValue::NUM ? static_cast<int>(b->num) : 0;
+        if (v != 4 && v != 8) {
+            *err = fmt("%s: layer %zu bits=%d (only 4 / 8)", path.c_str(), k, v);
+            return false;
+        }
+        const JValue* sc = e.get("scheme");
+        if (sc && (sc->kind != JValue::STR || sc->str != "per_channel")) {
+            *err = fmt("%s: layer %zu scheme %s: only per_channel weights run on the engine", path.c_str(), k,
+                        sc->kind == JValue::STR ? sc->str.c_str() : "(not a string)");
+            return false;
+        }
+        bits->push_back(v);
+    }
+    return true;
 }
 
 }  // namespace ptq8

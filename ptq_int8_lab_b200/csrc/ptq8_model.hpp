@@ -76,4 +76,9 @@ void quantize_weight_per_channel(const float* w, int cout, int k, int bits,
 
 int conv_out_dim(int in, int k, int s, int p);
 
+// Per-conv weight bits from a layer-plan JSON (the `layers` list of the
+// ptq-layer-plan/v1 schema, mixed_check.py:62-81 / mixed.py:179): exactly
+// n_conv entries in conv definition order, bits 4 or 8, scheme per_channel.
+bool load_layer_plan(const std::string& path, size_t n_conv, std::vector<int>* bits, std::string* err);
+
 }  // namespace ptq8

@@ -44,7 +44,18 @@ EXPORTS = (
     "ptq8_engine_forward_device", "ptq8_engine_input_buffer", "ptq8_engine_logits_buffer", "ptq8_engine_run", "ptq8_engine_copy_logits",
     "ptq8_engine_sync", "ptq8_engine_check_device_error", "ptq8_engine_tensor_info", "ptq8_engine_dump",
     "ptq8_engine_n_launches", "ptq8_engine_passes_log", "ptq8_engine_profile",
+    "ptq8_load", "ptq8_forward", "ptq8_forward_debug", "ptq8_capture_graph", "ptq8_destroy", "ptq8_last_error",
 )
+
+
+class Opts(ctypes.Structure):
+    """ptq8_opts of include/ptq8.h."""
+    _fields_ = [("device", ctypes.c_int), ("w_bits", ctypes.c_int), ("a_bits", ctypes.c_int),
+                ("act_mode", ctypes.c_int), ("passes", ctypes.c_int), ("max_batch", ctypes.c_int)]
+
+
+DUMP_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int8), ctypes.c_int,
+                           ctypes.c_int, ctypes.c_int, ctypes.c_int)
 
 
 class Ptq8Error(RuntimeError):
@@ -102,6 +113,12 @@ def lib() -> ctypes.CDLL:
         "ptq8_engine_profile": (c_int, [c_void_p, c_int, c_int, P(ctypes.c_float), P(ctypes.c_double),
                                         P(ctypes.c_double), P(c_int), c_int, P(c_int)]),
         "ptq8_engine_passes_log": (c_int, [c_void_p, c_char_p, c_size]),
+        "ptq8_load": (c_int, [c_char_p, c_char_p, c_char_p, P(Opts), P(c_void_p), c_char_p, c_size]),
+        "ptq8_forward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+        "ptq8_forward_debug": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, DUMP_FN, c_void_p]),
+        "ptq8_capture_graph": (c_int, [c_void_p, c_int]),
+        "ptq8_destroy": (None, [c_void_p]),
+        "ptq8_last_error": (c_char_p, [c_void_p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -4,6 +4,7 @@ Cases mirror 06-gpu-int8/cpp/ptq2_reader_test.cpp:113-245 and
 06-gpu-int8/cpp/ptq_model_test.cpp (format dispatch, EOF strictness, groups
 semantics, PTQC strictness)."""
 import ctypes
+import json
 import re
 import struct
 from pathlib import Path
@@ -168,3 +169,55 @@ def test_layer_plan(tmp_path):
     p.write_text(json.dumps({"layers": [{"name": "a", "bits": 4, "scheme": "per_group", "group_size": 32}]}))
     with pytest.raises(E.Ptq8Error, match="per_channel"):
         E.load_layer_plan(p, 1)
+
+
+# ---- one-call interface: ptq8_load / ptq8_destroy (host side; no GPU work before a forward)
+
+def _load_one(model, calib, plan=None, opts=None):
+    import ctypes
+    out = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(1024)
+    rc = E.lib().ptq8_load(str(model).encode(), str(calib).encode(), str(plan).encode() if plan else None,
+                           ctypes.byref(opts) if opts else None, ctypes.byref(out), err, len(err))
+    return rc, out, err.value.decode()
+
+
+def test_ptq8_load_good_and_destroy(make_model):
+    p = make_model(0)
+    opts = E.Opts(0, 8, 8, E.ACT_ABSMAX, 0, 0)
+    rc, eng, msg = _load_one(p["model"], p["calib"], p["plan"], opts)
+    assert rc == 0 and eng.value and msg == ""
+    E.lib().ptq8_destroy(eng)
+
+
+def test_ptq8_load_errors(make_model, tmp_path):
+    p = make_model(0)
+    rc, eng, msg = _load_one(tmp_path / "missing.bin", p["calib"])
+    assert rc != 0 and not eng.value and msg
+    bad = tmp_path / "plan.json"
+    cases = {
+        "{not json": "JSON",
+        '{"layers": []}': "'layers' must list 20 convs",
+        json.dumps({"layers": [{"bits": 6}] * 20}): "bits=6",
+        json.dumps({"layers": [{"bits": 4, "scheme": "per_group"}] * 20}): "only per_channel",
+        json.dumps({"layers": [{"bits": 8}] * 20}) + " x": "trailing data",
+    }
+    for text, want in cases.items():
+        bad.write_text(text)
+        rc, eng, msg = _load_one(p["model"], p["calib"], bad)
+        assert rc == 2 and not eng.value and want in msg, (text[:30], msg)   # PTQ8_ERR_FORMAT
+
+
+def test_ptq8_load_plan_matches_python_reader(make_model):
+    p = make_model(3)   # mixed W4 / W8 MobileNetV2
+    m = E.Model.load(p["model"])
+    want = E.load_layer_plan(p["plan"], m.n_conv)
+    assert 4 in want and 8 in want
+    rc, eng, msg = _load_one(p["model"], p["calib"], p["plan"])
+    assert rc == 0, msg
+    E.lib().ptq8_destroy(eng)
+
+
+def test_model_load_rejects_directory(tmp_path):
+    with pytest.raises(E.Ptq8Error, match="not a regular file"):
+        E.Model.load(tmp_path)
