@@ -587,6 +587,11 @@ int finalize(ptq8_engine* e, int max_batch) {
     int rc = plan(e);
     if (rc) return rc;
     const size_t NB = (size_t)max_batch;
+    // the kernels decode positions in 32-bit arithmetic
+    for (const Value& v : e->vals)
+        if (NB * (v.h + 2) * (v.w + 2) >= (size_t)1 << 31)
+            return e->fail(strf("max_batch %d too large for a %dx%d map (positions must stay below 2^31)", max_batch,
+                                v.h, v.w));
 
     // activation buffers
     for (size_t vi = 0; vi < e->vals.size(); ++vi) {
@@ -902,6 +907,10 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     }
     g.a_stage = st.a_stage;
     g.n_kchunks = st.n_kchunks;
+    g.fd_img = make_fastdiv((uint32_t)(g.Hp * g.Wp));
+    g.fd_wp = make_fastdiv((uint32_t)g.Wp);
+    g.fd_tiles_w = make_fastdiv((uint32_t)g.tiles_w);
+    g.fd_tiles_h = make_fastdiv((uint32_t)g.tiles_h);
     g.BN = st.bn;
     g.acc_cols = st.acc_cols;
     g.n_acc = n_acc_for(st.acc_cols);

@@ -613,6 +613,21 @@ __device__ __forceinline__ int8_t* code_ptr(const EpiParams& e, int o, size_t pq
 
 // ------------------------------------------------------------------ tensor-core conv
 
+// Division of 32-bit unsigned values by a fixed divisor d as one multiply-high:
+// with m = ceil(2^64 / d), x*m/2^64 = x/d + x*e/(d*2^64) for e = m*d - 2^64 < d,
+// and x*e/(d*2^64) < 2^-32 < 1/d, so the floor is exactly floor(x/d) for every
+// x < 2^32 (d = 1 is passed through).
+struct FastDiv {
+    unsigned long long m;
+    uint32_t d;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+    return {d <= 1 ? 0ull : (~0ull) / d + 1ull, d};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t x, const FastDiv& f) {
+    return f.d == 1 ? x : static_cast<uint32_t>(__umul64hi(static_cast<unsigned long long>(x), f.m));
+}
+
 struct ConvGeom {
     int mode;                   // 0: per-tap 4-D tile loads; 1: one halo block per tile, taps = shifted views
     int N, OH, OW;              // output map (per image)
@@ -641,6 +656,11 @@ struct ConvGeom {
     int aux_off;                // byte offset of the aux A tile (128 rows x 32 bytes) inside each A stage
     uint32_t aux_bytes;         // TMA bytes of that tile
     int aux_col;                // TMEM column of the aux accumulator inside a buffer
+    // divisors of the per-tile position decode
+    FastDiv fd_img;             // mode 1: Hp * Wp
+    FastDiv fd_wp;              // mode 1: Wp
+    FastDiv fd_tiles_w;         // mode 0: tiles along W
+    FastDiv fd_tiles_h;         // mode 0: tiles along H
 };
 
 constexpr int kEpiWarps = 16;                      // 4 per TMEM lane quadrant
@@ -744,12 +764,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         uint32_t ph = 0;
         for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
             int w0 = 0, h0 = 0, n0 = 0;
-            if (g.mode == 0) {
-                const int tw_i = mt % g.tiles_w;
-                const int rest = mt / g.tiles_w;
-                w0 = tw_i * g.TW;
-                h0 = (rest % g.tiles_h) * g.TH;
-                n0 = (rest / g.tiles_h) * g.TN;
+            if (MODE == 0) {
+                const uint32_t rest = fdiv(static_cast<uint32_t>(mt), g.fd_tiles_w);
+                const uint32_t nb = fdiv(rest, g.fd_tiles_h);
+                w0 = static_cast<int>(static_cast<uint32_t>(mt) - rest * g.fd_tiles_w.d) * g.TW;
+                h0 = static_cast<int>(rest - nb * g.fd_tiles_h.d) * g.TH;
+                n0 = static_cast<int>(nb) * g.TN;
             }
             int tap = 0, cc = 0;
             for (int ka = 0; ka < n_a; ++ka) {
@@ -873,22 +893,25 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const bool lower = RES ? e.post != 1 : e.act == 0;
         // output position of this thread's row r in M tile mt: image n, row h, column w,
         // bordered code row pq, fp32 row pf
+        // (bordered positions and tile indices stay below 2^32: the host limits the batch)
         auto position = [&](int mt, int& n, int& h, int& w, bool& valid, size_t& pq, size_t& pf) {
             if (MODE == 1) {
-                const size_t q = static_cast<size_t>(mt) * 128 + r;
-                const size_t img = static_cast<size_t>(g.Hp) * g.Wp;
-                n = static_cast<int>(q / img);
-                const int rem = static_cast<int>(q - static_cast<size_t>(n) * img);
-                h = rem / g.Wp - 1;
-                w = rem - (rem / g.Wp) * g.Wp - 1;
+                const uint32_t q = static_cast<uint32_t>(mt) * 128u + static_cast<uint32_t>(r);
+                const uint32_t nn = fdiv(q, g.fd_img);
+                const uint32_t rem = q - nn * g.fd_img.d;
+                const uint32_t hb = fdiv(rem, g.fd_wp);
+                n = static_cast<int>(nn);
+                h = static_cast<int>(hb) - 1;
+                w = static_cast<int>(rem - hb * g.fd_wp.d) - 1;
                 valid = n < g.N && h >= 0 && h < g.OH && w >= 0 && w < g.OW;
                 pq = q;
             } else {
-                const int tw_i = mt % g.tiles_w;
-                const int rest = mt / g.tiles_w;
-                n = (rest / g.tiles_h) * g.TN + rn;
-                h = (rest % g.tiles_h) * g.TH + rh;
-                w = tw_i * g.TW + rw;
+                const uint32_t rest = fdiv(static_cast<uint32_t>(mt), g.fd_tiles_w);
+                const uint32_t tw_i = static_cast<uint32_t>(mt) - rest * g.fd_tiles_w.d;
+                const uint32_t nb = fdiv(rest, g.fd_tiles_h);
+                n = static_cast<int>(nb) * g.TN + rn;
+                h = static_cast<int>(rest - nb * g.fd_tiles_h.d) * g.TH + rh;
+                w = static_cast<int>(tw_i) * g.TW + rw;
                 valid = in_tile && n < g.N && h < g.OH && w < g.OW;
                 pq = (static_cast<size_t>(n) * (g.OH + 2) + h + 1) * (g.OW + 2) + w + 1;
             }
