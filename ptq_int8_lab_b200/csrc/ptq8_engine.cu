@@ -837,14 +837,34 @@ EpiParams epi_for(ptq8_engine* e, const Step& st) {
     return p;
 }
 
+// Every kernel of the forward is launched with programmatic stream serialization:
+// it may be scheduled as soon as the previous kernel's blocks have passed their
+// set-up (griddepcontrol.launch_dependents), does its own set-up (barriers, TMEM,
+// resident weights, constants) meanwhile, and waits (griddepcontrol.wait) before
+// reading anything an earlier kernel wrote.
+template <typename... Params, typename... Args>
+void launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 // Launch step `si` (si == steps.size(): the pooling head) for batch n on the engine stream.
 void enqueue_step(ptq8_engine* e, int n, size_t si) {
     cudaStream_t s = e->stream;
     if (si == e->steps.size()) {
         const Value& fv = e->vals[e->final_val];
         const Model& m = *e->model;
-        head_kernel<<<n, 256, fv.c * sizeof(float), s>>>(fv.f32, fv.h * fv.w, fv.c, e->d_fc_w, e->d_fc_b, m.fc_out,
-                                                         e->d_logits);
+        launch_pdl(head_kernel, dim3(n), dim3(256), fv.c * sizeof(float), s, fv.f32, fv.h * fv.w, fv.c, e->d_fc_w,
+                   e->d_fc_b, m.fc_out, e->d_logits);
         return;
     }
     const Step& st = e->steps[si];
@@ -852,7 +872,8 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     if (st.kind == K_MAXPOOL) {
         const size_t total = (size_t)n * st.oh * st.ow * st.oc;
         const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 32);
-        maxpool_kernel<<<grid, 256, 0, s>>>(e->vals[st.in_val].f32, n, st.ih, st.iw, st.ic, st.oh, st.ow, ep);
+        launch_pdl(maxpool_kernel, dim3(grid), dim3(256), 0, s, e->vals[st.in_val].f32, n, st.ih, st.iw, st.ic, st.oh,
+                   st.ow, ep);
         return;
     }
     if (st.kind == K_DW) {
@@ -860,8 +881,8 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         const int8_t* in = vin.codes[vin.code_index(st.s_in)];
         const size_t total = (size_t)n * st.oh * st.ow * ((st.oc + 3) / 4);
         const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 64);
-        dw_conv_kernel<<<grid, 256, 0, s>>>(in, vin.ldq, st.d_w, n, st.ih, st.iw, st.oc, st.oh, st.ow, st.kh,
-                                            st.kw, st.sh, st.sw, st.ph, st.pw, ep);
+        launch_pdl(dw_conv_kernel, dim3(grid), dim3(256), 0, s, in, vin.ldq, st.d_w, n, st.ih, st.iw, st.oc, st.oh, st.ow,
+                   st.kh, st.kw, st.sh, st.sw, st.ph, st.pw, ep);
         return;
     }
     if (st.kind == K_STEM_IM2COL) {
@@ -873,9 +894,9 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         const int bands = (st.oh + rows - 1) / rows;
         const size_t band_bytes =
             (((size_t)c.cin * ((rows - 1) * c.sh + c.kh) * band_w + 15) & ~(size_t)15) + (size_t)st.kpad * sizeof(int);
-        stem_im2col_kernel<<<n * bands, 256, band_bytes, s>>>(e->d_input, st.d_im2col, n, c.cin, st.ih, st.iw, st.oh,
-                                                              st.ow, c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad,
-                                                              rows, (float)(1.0 / st.s_in), st.s_in);
+        launch_pdl(stem_im2col_kernel, dim3(n * bands), dim3(256), band_bytes, s, (const float*)e->d_input,
+                   st.d_im2col, n, c.cin, st.ih, st.iw, st.oh, st.ow, c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad, rows,
+                   (float)(1.0 / st.s_in), st.s_in);
     }
     ConvGeom g{};
     g.mode = st.mode;
@@ -934,7 +955,17 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         for (size_t c = 0; c < src.h_factor.size(); ++c) cc->aux_fb[c] = make_float2(src.h_factor[c], src.h_bias[c]);
     }
     void* args[7] = {&ma, &mb, &mxa, &mxb, &g, &ep, cc.get()};
-    cudaLaunchKernel(st.kfn, grid, dim3(kConvThreads), args, st.smem, s);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kConvThreads);
+    cfg.dynamicSmemBytes = st.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelExC(&cfg, st.kfn, args);
 }
 
 int enqueue(ptq8_engine* e, int n) {

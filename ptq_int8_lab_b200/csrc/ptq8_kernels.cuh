@@ -122,6 +122,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* m, 
         : "memory");
 }
 
+// Programmatic dependent launch: the forward's kernels are launched so that the
+// next one may start while this one drains.  launch_dependents lets it be
+// scheduled; wait blocks until every earlier kernel of the stream has completed
+// and its memory is visible -- executed before the first read of anything an
+// earlier kernel wrote.  (Both are no-ops without the launch attribute.)
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -743,6 +751,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    griddep_launch();
     const uint32_t tmem = tslot;
     const int n_a = MODE == 1 ? g.n_cchunks : g.n_kchunks;   // A loads per tile
 
@@ -762,6 +771,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
         int s = 0;
         uint32_t ph = 0;
+        griddep_wait();   // A tiles (and the aux rows) are earlier kernels' outputs
         for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
             int w0 = 0, h0 = 0, n0 = 0;
             if (MODE == 0) {
@@ -891,6 +901,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         constexpr int n_out = NOUT;
         // codes can only saturate low when the values are not already clipped at zero
         const bool lower = RES ? e.post != 1 : e.act == 0;
+        griddep_wait();   // residuals are earlier kernels' outputs
         // output position of this thread's row r in M tile mt: image n, row h, column w,
         // bordered code row pq, fp32 row pf
         // (bordered positions and tile indices stay below 2^32: the host limits the batch)
@@ -1075,6 +1086,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restrict__ out, int N, int C, int H,
                                    int W, int OH, int OW, int KH, int KW, int SH, int SW, int PH, int PW,
                                    int kpad, int rows, float inv, double s) {
+    griddep_launch();
+    griddep_wait();
     extern __shared__ __align__(16) int8_t band[];   // [C][band_h][band_w], then int koff[kpad]
     const int bands = (OH + rows - 1) / rows;
     const int n = blockIdx.x / bands;
@@ -1141,6 +1154,8 @@ __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restri
 __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int8_t* __restrict__ w, int N, int H,
                                int W, int C, int OH, int OW, int KH, int KW, int SH, int SW, int PH, int PW,
                                const EpiParams e) {
+    griddep_launch();
+    griddep_wait();
     const int cq = (C + 3) / 4;
     const size_t total = static_cast<size_t>(N) * OH * OW * cq;
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -1197,6 +1212,8 @@ __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int
 // values and then quantizing equals the reference's order (ref_e2e.py:192-203).
 __global__ void maxpool_kernel(const float* __restrict__ in, int N, int H, int W, int C, int OH, int OW,
                                const EpiParams e) {
+    griddep_launch();
+    griddep_wait();
     const size_t total = static_cast<size_t>(N) * OH * OW * C;
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -1250,6 +1267,8 @@ __global__ void quantize_kernel(const float* __restrict__ x, size_t n, QParams q
 // One CTA per image: fixed-order fp32 position sums, float64 FC accumulation.
 __global__ void head_kernel(const float* __restrict__ x, int HW, int C, const float* __restrict__ fc_w,
                             const float* __restrict__ fc_b, int n_out, float* __restrict__ logits) {
+    griddep_launch();
+    griddep_wait();
     extern __shared__ float pooled[];
     const int n = blockIdx.x;
     const size_t p0 = static_cast<size_t>(n) * HW;
