@@ -821,6 +821,10 @@ EpiParams epi_for(ptq8_engine* e, const Step& st) {
     }
     p.act = st.act;
     p.post = st.res_val >= 0 ? st.post : 0;
+    if (st.conv >= 0) {   // |acc| <= K * 128 * 128: below 2^22 for K < 256
+        const ConvSpec& c = e->q[st.conv].spec;
+        p.acc_small = c.in_channels() * c.kh * c.kw < 256 ? 1 : 0;
+    }
     p.out_q0 = out.codes.size() > 0 ? out.codes[0] : nullptr;
     p.out_q1 = out.codes.size() > 1 ? out.codes[1] : nullptr;
     p.ldq0 = p.ldq1 = out.ldq;

@@ -490,6 +490,7 @@ struct EpiParams {
     int vec32;  // 1 when cout % 8 == 0: tiled fp32 maps, 256-bit loads/stores of 8 channels
     int act;    // activation of the conv itself: 0 none / 1 relu / 2 relu6
     int aux_act;   // AUX: activation of the recomputed residual (its constants are in ConvConsts)
+    int acc_small; // 1 when K * 128 * 128 < 2^22: accumulators convert to float without a range check
     int post;   // residual: 0 none, 1 add then relu, 2 add only
     // positional decomposition: channel c' = pos*dcr_oc + c of a 1x1 GEMM output is code
     // (pos / dcr_w, pos % dcr_w, c) of a dcr_h x dcr_w map (DepthToSpace, DCR order)
@@ -545,12 +546,14 @@ __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0
 // |acc| < 2^22 (exact subtraction afterwards); in that range the pattern xor
 // 0x4B000000 stays below 2^23, so one OR over the 16 patterns tells whether
 // every accumulator was in range.  Otherwise the rounding conversion is used.
-__device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float2* fb, int act, float (&y)[16]) {
+// `check` false: the caller knows |acc| < 2^22 (K * 128 * 128 < 2^22, i.e. K < 256).
+__device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float2* fb, int act, float (&y)[16],
+                                          bool check = true) {
     uint32_t range = 0;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
         const uint32_t bits = v[j] + static_cast<uint32_t>(kRoundMagicBits);
-        range |= bits ^ 0x4B000000u;
+        if (check) range |= bits ^ 0x4B000000u;
         y[j] = __uint_as_float(bits);
     }
     if (range < 0x800000u) {
@@ -942,10 +945,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 fbr[j] = cc.fb[ch + j];
                 if (AUX) afbr[j] = cc.aux_fb[ch + j];
             }
-            int t = 0;
-            for (int mt = blockIdx.x; mt < g.m_tiles; mt += gridDim.x, ++t) {
-                const int buf = t % NA;
-                const uint32_t use = static_cast<uint32_t>(t / NA);
+            int buf = 0;
+            uint32_t use = 0;   // parity of the current use of accumulator `buf`
+            for (int mt = blockIdx.x; mt < g.m_tiles; mt += gridDim.x) {
                 int n, h, w;
                 bool valid;
                 size_t pq, pf;
@@ -966,8 +968,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     tmem_wait_ld();
                     if (valid) {
                         float y[16];
-                        dequant16(v, fbr, e.act, y);
-                        if (AUX) dequant16(vx, afbr, e.aux_act, res);
+                        dequant16(v, fbr, e.act, y, !e.acc_small);
+                        if (AUX) dequant16(vx, afbr, e.aux_act, res, false);   // aux K = 32
                         finish16<RES, F32>(e, pf, ch, nv, y, res);
 #pragma unroll
                         for (int o = 0; o < 2; ++o) {
@@ -990,12 +992,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_relaxed(acce0 + 8 * buf);
+                if (++buf == NA) {
+                    buf = 0;
+                    use ^= 1u;
+                }
             }
         } else {
-        int t = gi;
-        for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NG * gridDim.x, t += NG) {
-            const int buf = t % NA;
-            const uint32_t use = static_cast<uint32_t>(t / NA);
+        // tiles t = gi, gi + NG, ...: accumulator t % NA (NG divides NA), parity (t / NA) & 1
+        int buf = gi;
+        uint32_t use = 0;
+        for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NG * gridDim.x) {
             int n, h, w;
             bool valid;
             size_t pq, pf;
@@ -1028,8 +1034,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const int nv = min(16, tile_end - ch);
                     if (!valid || nv <= 0) continue;
                     float y[16];
-                    dequant16(v, cc.fb + ch, e.act, y);
-                    if (AUX) dequant16(vx, cc.aux_fb + ch, e.aux_act, res);
+                    dequant16(v, cc.fb + ch, e.act, y, !e.acc_small);
+                    if (AUX) dequant16(vx, cc.aux_fb + ch, e.aux_act, res, false);   // aux K = 32
                     finish16<RES, F32>(e, pf, ch, nv, y, res);
                     // prefetch the next residual half of this warp
                     {
@@ -1065,6 +1071,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_relaxed(acce0 + 8 * buf);
+            if ((buf += NG) >= NA) {
+                buf -= NA;
+                use ^= 1u;
+            }
         }
         }
     }
