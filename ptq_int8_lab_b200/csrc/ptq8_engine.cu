@@ -68,6 +68,10 @@ struct Value {
     int ldq = 0;                 // code row pitch (c rounded up to 32)
     float* f32 = nullptr;
     std::vector<int8_t*> codes;  // one per scale
+    std::vector<char> sub2;      // per scale: codes kept only at even (h, w), half-size bordered map
+    int sub_h() const { return (h + 1) / 2; }
+    int sub_w() const { return (w + 1) / 2; }
+    bool is_sub(int k) const { return k >= 0 && k < (int)sub2.size() && sub2[k]; }
     int code_index(double s) const {
         for (size_t i = 0; i < scales.size(); ++i)
             if (scales[i] == s) return (int)i;
@@ -107,7 +111,9 @@ struct Step {
     CUtensorMap map_a{}, map_b{};
     // aux GEMM: this conv recomputes its residual (the stem's output) from the
     // stem's im2col rows instead of reading a stored fp32 map
-    int aux_src = -1;      // step index of the stem, -1 none
+    int aux_src = -1;      // step index of the recomputed conv (stem or fused downsample), -1 none
+    int aux_kb = 32;       // K bytes of that GEMM
+    bool fused = false;    // a downsample computed inside its block's last conv: never launched
     int aux_off = 0;       // byte offset of the aux tile inside an A stage
     int acc_cols = 0;      // TMEM columns per accumulator buffer (main + aux)
     CUtensorMap map_xa{}, map_xb{};
@@ -317,6 +323,8 @@ void tile_shape(int N, int OH, int OW, int* TW, int* TH, int* TN) {
     (void)N;
 }
 
+constexpr size_t kSmemBudget = 225 * 1024;
+
 int choose_cb(int cpad) { return cpad % 128 == 0 ? 128 : (cpad % 64 == 0 ? 64 : 32); }
 
 // N tile: the whole Cout when it fits one MMA (N <= 256, multiple of 16);
@@ -333,6 +341,37 @@ void choose_bn(int cout, int* bn, int* ntiles) {
     nt = (cout + b - 1) / b;
     *ntiles = nt;
     *bn = b;
+}
+
+// Whether the downsample `ds` (1x1 stride 2, no activation) of a block can run
+// inside the block's last conv `ci` as its aux GEMM: `ci` is a 3x3 stride-1
+// "same" conv on the downsample's output map in halo-block mode, N tile = all
+// channels (<= 128, so main + aux accumulators fit twice in TMEM), and the
+// block input is produced by a tensor-core conv (its epilogue writes the
+// subsampled codes the aux GEMM reads).
+bool ds_fusable(const ptq8_engine* e, int ds, int ci, int in_val) {
+    const ConvSpec& d = e->q[ds].spec;
+    const ConvSpec& c = e->q[ci].spec;
+    if (e->q[ds].view_oh > 0 || d.groups != 1 || d.kh != 1 || d.kw != 1 || d.sh != 2 || d.sw != 2 || d.ph != 0 ||
+        d.pw != 0 || d.relu != 0)
+        return false;
+    const int kb = round_up(d.cin, 32);
+    if (kb > 128) return false;
+    if (e->q[ci].view_oh > 0 || c.groups != 1 || c.kh != 3 || c.kw != 3 || c.sh != 1 || c.sw != 1 || c.ph != 1 ||
+        c.pw != 1)
+        return false;
+    if (c.cout != d.cout || c.cout > 128 || c.cout % 16 != 0 || round_up(c.cin, 32) % 64 != 0) return false;
+    const Value& x = e->vals[in_val];
+    const int oh = (x.h + 1) / 2, ow = (x.w + 1) / 2;
+    if (oh * ow < 64 || 128 + 2 * (ow + 2) + 2 > 256) return false;
+    // halo-block pipeline with resident weights and two stages must fit in shared memory
+    const int cpad = round_up(c.cin, 32), cb = choose_cb(cpad), bn = round_up(c.cout, 16);
+    const size_t b_res = (size_t)9 * (cpad / cb) * round_up(bn * cb, 1024);
+    const size_t stage = (size_t)round_up((128 + 2 * (ow + 2) + 2) * cb, 1024) + 128 * kb;
+    if (1024 + 2 * stage + b_res + (size_t)round_up(bn * kb, 1024) > kSmemBudget) return false;
+    for (const Step& st : e->steps)
+        if (st.out_val == in_val) return st.kind == K_TC || st.kind == K_STEM_IM2COL;
+    return false;
 }
 
 // Whether the block conv `ci`, whose residual is the stem's output, can recompute
@@ -430,17 +469,19 @@ int plan(ptq8_engine* e) {
             if (ci >= 0) cs.push_back(ci);
         int ident = -1;
         bool fuse = false;
+        int ds_step = -1;
         if (b.residual != 0) {
             if (b.ds >= 0) {
                 int dv;
                 rc = add_conv(b.ds, cur, &dv, -1, 0);
                 if (rc) return rc;
                 ident = dv;
+                if (!cs.empty() && ds_fusable(e, b.ds, cs.back(), cur)) ds_step = (int)e->steps.size() - 1;
             } else {
                 ident = cur;
             }
             fuse = ident == stem_val && !cs.empty() && stem_identity_fusable(e, cs.back());
-            if (!fuse) e->vals[ident].need_f32 = true;
+            if (!fuse && ds_step < 0) e->vals[ident].need_f32 = true;
         }
         int t = cur;
         for (size_t k = 0; k < cs.size(); ++k) {
@@ -448,10 +489,36 @@ int plan(ptq8_engine* e) {
             int ov;
             rc = add_conv(cs[k], t, &ov, last && b.residual ? ident : -1, last ? b.residual : 0);
             if (rc) return rc;
-            if (last && fuse) e->steps.back().aux_src = stem_step;
+            if (last && fuse) {
+                e->steps.back().aux_src = stem_step;
+                e->steps.back().aux_kb = 32;
+            }
+            if (last && ds_step >= 0) {
+                e->steps.back().aux_src = ds_step;
+                e->steps.back().aux_kb = round_up(e->q[b.ds].spec.cin, 32);
+                e->steps[ds_step].fused = true;
+            }
             t = ov;
         }
         cur = t;
+    }
+    // a fused downsample reads its input codes subsampled: its slot must be its own
+    for (Step& ds : e->steps) {
+        if (!ds.fused) continue;
+        Value& x = e->vals[ds.in_val];
+        const int k = x.code_index(ds.s_in);
+        bool shared = false;
+        for (const Step& o : e->steps)
+            if (&o != &ds && o.in_val == ds.in_val && o.kind != K_MAXPOOL && o.s_in == ds.s_in) shared = true;
+        if (shared) {   // undo: run the downsample as its own launch
+            ds.fused = false;
+            for (Step& c : e->steps)
+                if (c.aux_src == (int)(&ds - &e->steps[0])) c.aux_src = -1;
+            e->vals[ds.out_val].need_f32 = true;
+            continue;
+        }
+        x.sub2.resize(x.scales.size(), 0);
+        x.sub2[k] = 1;
     }
     e->vals[cur].need_f32 = true;
     e->final_val = cur;
@@ -479,7 +546,6 @@ bool make_map(ptq8_engine* e, CUtensorMap* map, CUtensorMapDataType dt, int rank
     return true;
 }
 
-constexpr size_t kSmemBudget = 225 * 1024;
 
 // conv_tc_kernel specializations: [K-chunk 32/64/128][mode][code outputs][residual][fp32 out]
 void* g_conv_table[3][2][3][2][2];
@@ -518,10 +584,10 @@ void fill_table() {
 
 int cb_index(int cb) { return cb == 128 ? 2 : (cb == 64 ? 1 : 0); }
 
-// Dynamic shared memory of conv_tc_kernel for a pipeline shape (aux: + aux weights [bn][32]).
-size_t conv_smem_bytes(int a_stage, int cb, int bn, int stages, int b_chunks, bool aux = false) {
+// Dynamic shared memory of conv_tc_kernel for a pipeline shape (aux_kb > 0: + aux weights [bn][aux_kb]).
+size_t conv_smem_bytes(int a_stage, int cb, int bn, int stages, int b_chunks, int aux_kb = 0) {
     const size_t sb = (size_t)round_up(bn * cb, 1024);
-    return 1024 + (size_t)stages * a_stage + (size_t)b_chunks * sb + (aux ? (size_t)round_up(bn * 32, 1024) : 0);
+    return 1024 + (size_t)stages * a_stage + (size_t)b_chunks * sb + (aux_kb ? (size_t)round_up(bn * aux_kb, 1024) : 0);
 }
 
 // Keep the whole weight slab of the N tile resident when it fits next to a
@@ -531,7 +597,7 @@ bool choose_pipeline(Step& st, int min_res) {
     for (int S : {24, 20, 16, 12, 10, 8, 6, 5, 4, 3, 2}) {
         if (S < min_res) break;
         if ((size_t)S * st.a_stage > 96 * 1024 && S > min_res) continue;   // ~96 KB of A in flight is plenty
-        const size_t b = conv_smem_bytes(st.a_stage, st.cb, st.bn, S, st.n_kchunks, st.aux_src >= 0);
+        const size_t b = conv_smem_bytes(st.a_stage, st.cb, st.bn, S, st.n_kchunks, st.aux_src >= 0 ? st.aux_kb : 0);
         if (b <= kSmemBudget) {
             st.stages = S;
             st.b_resident = 1;
@@ -602,9 +668,10 @@ int finalize(ptq8_engine* e, int max_batch) {
         // fp32 maps use the f32_off layout: whole 32-position blocks
         if (v.need_f32 && !e->dalloc(&v.f32, ((pix + 31) & ~(size_t)31) * v.c * sizeof(float), "alloc fp32 activation"))
             return PTQ8_ERR_CUDA;
-        // int8 codes carry a one-pixel zero border (written once, never touched again)
-        const size_t bpix = NB * (v.h + 2) * (v.w + 2);
+        // int8 codes carry a one-pixel zero border (written once, never touched again);
+        // subsampled slots hold the even positions only, in a half-size bordered map
         for (size_t k = 0; k < v.scales.size(); ++k) {
+            const size_t bpix = v.is_sub((int)k) ? NB * (v.sub_h() + 2) * (v.sub_w() + 2) : NB * (v.h + 2) * (v.w + 2);
             if (!e->dalloc(&v.codes[k], bpix * v.ldq, "alloc int8 codes")) return PTQ8_ERR_CUDA;
             if (!e->cuda_ok(cudaMemset(v.codes[k], 0, bpix * v.ldq), "clear codes")) return PTQ8_ERR_CUDA;
         }
@@ -677,6 +744,7 @@ int finalize(ptq8_engine* e, int max_batch) {
             return e->fail(strf("conv[%d]: N tile %d breaks the 32-byte store alignment", st.conv, st.bn));
         if (!e->dalloc(&st.d_w, w.size(), "alloc weights")) return PTQ8_ERR_CUDA;
         cudaMemcpy(st.d_w, w.data(), w.size(), cudaMemcpyHostToDevice);
+        if (st.fused) continue;   // weights and constants are read by the conv that computes it
         {
             cuuint64_t dims[2] = {(cuuint64_t)st.ktot, (cuuint64_t)c.cout};
             cuuint64_t strides[1] = {(cuuint64_t)st.ktot};
@@ -699,15 +767,15 @@ int finalize(ptq8_engine* e, int max_batch) {
             if (st.blk_rows <= 256) {
                 st.mode = 1;
                 st.a_stage = round_up(st.blk_rows * st.cb, 1024);
-                if (st.aux_src >= 0) {   // + the aux tile: 128 im2col rows of 32 bytes
+                if (st.aux_src >= 0) {   // + the aux tile: 128 rows of aux_kb bytes
                     st.aux_off = st.a_stage;
-                    st.a_stage += 128 * 32;
+                    st.a_stage += 128 * st.aux_kb;
                 }
                 if (!choose_pipeline(st, 2)) st.mode = 0;
             }
         }
         if (st.aux_src >= 0 && (st.mode != 1 || st.n_ntiles != 1 || (st.cb != 64 && st.cb != 128)))
-            return e->fail(strf("conv[%d]: stem identity fusion needs the halo-block pipeline", st.conv));
+            return e->fail(strf("conv[%d]: residual fusion needs the halo-block pipeline", st.conv));
         st.acc_cols = acc_cols_for(st.bn) * (st.aux_src >= 0 ? 2 : 1);
         if (st.mode == 0) {
             st.a_stage = 128 * st.cb;
@@ -737,21 +805,39 @@ int finalize(ptq8_engine* e, int max_batch) {
                           swizzle_for(st.cb)))
                 return PTQ8_ERR_CUDA;
             if (st.aux_src >= 0) {
-                // the stem's bordered im2col rows line up with this conv's bordered tile rows
+                // aux rows aligned with this conv's bordered tile rows: the stem's bordered
+                // im2col rows, or the subsampled block-input codes of a fused downsample
                 const Step& src = e->steps[st.aux_src];
-                if (src.oh != vin.h || src.ow != vin.w || src.kpad != 32 || !src.d_im2col || !src.d_w)
-                    return e->fail(strf("conv[%d]: stem identity fusion geometry mismatch", st.conv));
-                cuuint64_t xdims[2] = {32, rows};
-                cuuint64_t xstr[1] = {32};
-                cuuint32_t xbox[2] = {32, 128};
-                if (!make_map(e, &st.map_xa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, src.d_im2col, xdims, xstr, xbox, estr,
-                              swizzle_for(32)))
+                const int kb = st.aux_kb;
+                void* xbase = nullptr;
+                cuuint64_t xc = 0, xld = 0;
+                if (src.kind == K_STEM_IM2COL) {
+                    if (src.oh != vin.h || src.ow != vin.w || src.kpad != 32 || kb != 32 || !src.d_im2col)
+                        return e->fail(strf("conv[%d]: stem identity fusion geometry mismatch", st.conv));
+                    xbase = src.d_im2col;
+                    xc = 32;
+                    xld = 32;
+                } else {
+                    const Value& x = e->vals[src.in_val];
+                    const int k = x.code_index(src.s_in);
+                    if (!x.is_sub(k) || x.sub_h() != vin.h || x.sub_w() != vin.w || round_up(x.c, 32) != kb)
+                        return e->fail(strf("conv[%d]: downsample fusion geometry mismatch", st.conv));
+                    xbase = x.codes[k];
+                    xc = (cuuint64_t)x.c;
+                    xld = (cuuint64_t)x.ldq;
+                }
+                if (!src.d_w) return e->fail(strf("conv[%d]: aux weights missing", st.conv));
+                cuuint64_t xdims[2] = {xc, rows};
+                cuuint64_t xstr[1] = {xld};
+                cuuint32_t xbox[2] = {(cuuint32_t)kb, 128};
+                if (!make_map(e, &st.map_xa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xbase, xdims, xstr, xbox, estr,
+                              swizzle_for(kb)))
                     return PTQ8_ERR_CUDA;
                 cuuint64_t wdims[2] = {(cuuint64_t)src.ktot, (cuuint64_t)e->q[src.conv].spec.cout};
                 cuuint64_t wstr[1] = {(cuuint64_t)src.ktot};
-                cuuint32_t wbox[2] = {32, (cuuint32_t)st.bn};
+                cuuint32_t wbox[2] = {(cuuint32_t)kb, (cuuint32_t)st.bn};
                 if (!make_map(e, &st.map_xb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, src.d_w, wdims, wstr, wbox, estr,
-                              swizzle_for(32)))
+                              swizzle_for(kb)))
                     return PTQ8_ERR_CUDA;
             }
         } else {
@@ -775,7 +861,7 @@ int finalize(ptq8_engine* e, int max_batch) {
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, e->device);
         for (Step& st : e->steps) {
-            if (st.kind != K_TC && st.kind != K_STEM_IM2COL) continue;
+            if ((st.kind != K_TC && st.kind != K_STEM_IM2COL) || st.fused) continue;
             const Value& out = e->vals[st.out_val];
             const int nout = (int)out.scales.size();
             const int res = st.res_val >= 0 ? 1 : 0;
@@ -828,6 +914,10 @@ EpiParams epi_for(ptq8_engine* e, const Step& st) {
     p.out_q0 = out.codes.size() > 0 ? out.codes[0] : nullptr;
     p.out_q1 = out.codes.size() > 1 ? out.codes[1] : nullptr;
     p.ldq0 = p.ldq1 = out.ldq;
+    for (int k = 0; k < 2; ++k)
+        if (out.is_sub(k)) p.sub_mask |= 1 << k;
+    p.sub_h = out.sub_h();
+    p.sub_w = out.sub_w();
     if (out.scales.size() > 0) {
         p.s0 = out.scales[0];
         p.inv0 = (float)(1.0 / out.scales[0]);
@@ -872,6 +962,7 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         return;
     }
     const Step& st = e->steps[si];
+    if (st.fused) return;   // computed inside its block's last conv
     EpiParams ep = epi_for(e, st);
     if (st.kind == K_MAXPOOL) {
         const size_t total = (size_t)n * st.oh * st.ow * st.oc;
@@ -943,7 +1034,8 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     if (st.aux_src >= 0) {
         const Step& src = e->steps[st.aux_src];
         g.aux_off = st.aux_off;
-        g.aux_bytes = 128 * 32;
+        g.aux_bytes = (uint32_t)(128 * st.aux_kb);
+        g.aux_kb = st.aux_kb;
         g.aux_col = acc_cols_for(st.bn);
         ep.aux_act = src.act;
     }
@@ -989,13 +1081,21 @@ void step_work(const ptq8_engine* e, int n, size_t si, double* macs, double* byt
         return;
     }
     const Step& st = e->steps[si];
-    const Value& out = e->vals[st.out_val];
-    double outb = (double)n * out.h * out.w * out.c * ((out.need_f32 ? 4.0 : 0.0) + (double)out.scales.size());
-    // residual: the stored fp32 map, or (aux GEMM) the stem's bordered im2col rows
-    double resb = st.res_val < 0 ? 0.0
-                  : st.aux_src >= 0 ? (double)n * (out.h + 2) * (out.w + 2) * 32.0
-                                    : (double)n * out.h * out.w * out.c * 4.0;
     *kind = st.kind;
+    if (st.fused) {   // counted with the conv that computes it
+        *macs = 0;
+        *bytes = 0;
+        return;
+    }
+    const Value& out = e->vals[st.out_val];
+    double outb = 0;
+    for (size_t k = 0; k < out.scales.size(); ++k)
+        outb += (double)n * (out.is_sub((int)k) ? out.sub_h() * out.sub_w() : out.h * out.w) * out.c;
+    if (out.need_f32) outb += (double)n * out.h * out.w * out.c * 4.0;
+    // residual: the stored fp32 map, or (aux GEMM) the aux rows (stem im2col / subsampled codes)
+    double resb = st.res_val < 0 ? 0.0
+                  : st.aux_src >= 0 ? (double)n * (out.h + 2) * (out.w + 2) * st.aux_kb
+                                    : (double)n * out.h * out.w * out.c * 4.0;
     if (st.kind == K_MAXPOOL) {
         *macs = 0;
         *bytes = (double)n * st.ih * st.iw * st.ic * 4.0 + outb;
@@ -1007,6 +1107,11 @@ void step_work(const ptq8_engine* e, int n, size_t si, double* macs, double* byt
     const double inb = st.kind == K_STEM_IM2COL ? (double)n * st.ih * st.iw * st.ic * 4.0
                                                 : (double)n * st.ih * st.iw * st.ic;
     *bytes = inb + (double)c.cout * c.cin * c.kh * c.kw + outb + resb;
+    if (st.aux_src >= 0 && e->steps[st.aux_src].fused) {   // the downsample's GEMM runs here
+        const ConvSpec& d = e->q[e->steps[st.aux_src].conv].spec;
+        *macs += pos * d.cout * (double)d.cin;
+        *bytes += (double)d.cout * d.cin;
+    }
 }
 
 // The CUDA graph of one forward at batch n (captured on first use, then cached).
@@ -1529,9 +1634,13 @@ int ptq8_engine_tensor_info(ptq8_engine* e, int what, int index, int* shape4) {
         const Step& st = e->steps[e->conv_step[index]];
         if (st.kind == K_STEM_IM2COL) {
             shape4[0] = e->max_batch; shape4[1] = st.oh; shape4[2] = st.ow; shape4[3] = st.kpad;
-        } else {
+        } else {   // a fused downsample reads (and reports) the even positions only
             const Value& v = e->vals[st.in_val];
-            shape4[0] = e->max_batch; shape4[1] = v.h; shape4[2] = v.w; shape4[3] = v.ldq;
+            const bool sub = v.is_sub(v.code_index(st.s_in));
+            shape4[0] = e->max_batch;
+            shape4[1] = sub ? v.sub_h() : v.h;
+            shape4[2] = sub ? v.sub_w() : v.w;
+            shape4[3] = v.ldq;
         }
         return PTQ8_OK;
     }
@@ -1566,13 +1675,15 @@ int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst,
                 return PTQ8_OK;
             }
             const Value& v = e->vals[st.in_val];
-            const int8_t* src = v.codes[v.code_index(st.s_in)];
+            const int k = v.code_index(st.s_in);
+            const int8_t* src = v.codes[k];
+            const int H = v.is_sub(k) ? v.sub_h() : v.h, W = v.is_sub(k) ? v.sub_w() : v.w;
             // drop the one-pixel border: per image, H rows of W*ld bytes out of (H+2) x (W+2)*ld
-            const size_t row = (size_t)v.w * v.ldq, prow = (size_t)(v.w + 2) * v.ldq;
+            const size_t row = (size_t)W * v.ldq, prow = (size_t)(W + 2) * v.ldq;
             for (int i = 0; i < n; ++i) {
-                const int8_t* s0 = src + ((size_t)i * (v.h + 2) + 1) * prow + v.ldq;
-                int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * v.h * row;
-                if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, v.h, cudaMemcpyDeviceToHost), "dump"))
+                const int8_t* s0 = src + ((size_t)i * (H + 2) + 1) * prow + v.ldq;
+                int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * H * row;
+                if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, H, cudaMemcpyDeviceToHost), "dump"))
                     return PTQ8_ERR_CUDA;
             }
             return PTQ8_OK;
@@ -1634,7 +1745,7 @@ int ptq8_engine_profile(ptq8_engine* e, int n, int iters, float* ms, double* mac
 int ptq8_engine_n_launches(const ptq8_engine* e) {
     if (!e || !e->planned) return -1;
     int k = 1;   // head
-    for (const Step& st : e->steps) k += st.kind == K_STEM_IM2COL ? 2 : 1;
+    for (const Step& st : e->steps) k += st.fused ? 0 : st.kind == K_STEM_IM2COL ? 2 : 1;
     return k;
 }
 

@@ -490,6 +490,10 @@ struct EpiParams {
     int vec32;  // 1 when cout % 8 == 0: tiled fp32 maps, 256-bit loads/stores of 8 channels
     int act;    // activation of the conv itself: 0 none / 1 relu / 2 relu6
     int aux_act;   // AUX: activation of the recomputed residual (its constants are in ConvConsts)
+    // bit o set: code output o is written only at even (h, w), into a bordered
+    // (sub_h+2) x (sub_w+2) map at (h/2, w/2) -- the input of a fused 1x1 stride-2 conv
+    int sub_mask;
+    int sub_h, sub_w;
     int acc_small; // 1 when K * 128 * 128 < 2^22: accumulators convert to float without a range check
     int post;   // residual: 0 none, 1 add then relu, 2 add only
     // positional decomposition: channel c' = pos*dcr_oc + c of a 1x1 GEMM output is code
@@ -611,10 +615,18 @@ __device__ __forceinline__ void finish16(const EpiParams& e, size_t pf, int c0, 
     }
 }
 
-// Code row of output o for channel c0 (bordered layout; positional decomposition remaps).
-__device__ __forceinline__ int8_t* code_ptr(const EpiParams& e, int o, size_t pq, int n, int c0) {
+// Whether output o keeps the code of position (h, w) (subsampled outputs keep even positions).
+__device__ __forceinline__ bool code_kept(const EpiParams& e, int o, int h, int w) {
+    return !((e.sub_mask >> o) & 1) || ((h | w) & 1) == 0;
+}
+
+// Code row of output o for channel c0 (bordered layout; positional decomposition remaps;
+// subsampled outputs address the half-size map).
+__device__ __forceinline__ int8_t* code_ptr(const EpiParams& e, int o, size_t pq, int n, int c0, int h, int w) {
     int cq = c0;
-    if (e.dcr_oc) {
+    if ((e.sub_mask >> o) & 1) {
+        pq = (static_cast<size_t>(n) * (e.sub_h + 2) + (h >> 1) + 1) * (e.sub_w + 2) + (w >> 1) + 1;
+    } else if (e.dcr_oc) {
         const int pos = c0 / e.dcr_oc;
         cq = c0 - pos * e.dcr_oc;
         pq = (static_cast<size_t>(n) * (e.dcr_h + 2) + pos / e.dcr_w + 1) * (e.dcr_w + 2) + pos % e.dcr_w + 1;
@@ -660,12 +672,13 @@ struct ConvGeom {
     int stages;                 // A (and streamed B) pipeline depth, <= kMaxStages
     int b_resident;             // 1: the CTA's whole weight slab stays in shared memory
     uint32_t a_bytes, b_bytes;  // TMA bytes per A stage / per B chunk
-    // aux GEMM (AUX kernels): a second 1x1 GEMM with K = 32 bytes per row, over
-    // rows aligned with the tile's rows, into a second accumulator; its
-    // dequantized output is the residual (a block identity recomputed instead
-    // of stored in fp32)
-    int aux_off;                // byte offset of the aux A tile (128 rows x 32 bytes) inside each A stage
+    // aux GEMM (AUX kernels): a second 1x1 GEMM with K = aux_kb (32, 64 or 128)
+    // bytes per row, over rows aligned with the tile's rows, into a second
+    // accumulator; its dequantized output is the residual (a block identity
+    // recomputed instead of stored in fp32)
+    int aux_off;                // byte offset of the aux A tile (128 rows x aux_kb bytes) inside each A stage
     uint32_t aux_bytes;         // TMA bytes of that tile
+    int aux_kb;                 // K bytes of the aux GEMM (its swizzle width)
     int aux_col;                // TMEM column of the aux accumulator inside a buffer
     // divisors of the per-tile position decode
     FastDiv fd_img;             // mode 1: Hp * Wp
@@ -713,7 +726,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int sb_stride = (BN * CB + 1023) & ~1023;   // every B chunk 1024-byte aligned (swizzle atoms)
     uint8_t* sA = smem;
     uint8_t* sB = smem + S * g.a_stage;
-    uint8_t* sBx = sB + (g.b_resident ? g.n_kchunks : S) * sb_stride;   // aux weights [BN][32] (AUX)
+    uint8_t* sBx = sB + (g.b_resident ? g.n_kchunks : S) * sb_stride;   // aux weights [BN][aux_kb] (AUX)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -765,7 +778,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         bool ok = true;
         if (g.b_resident) {
             if (elect_one()) {
-                mbar_expect_tx(bfull, g.b_bytes * g.n_kchunks + (AUX ? static_cast<uint32_t>(BN * 32) : 0u));
+                mbar_expect_tx(bfull, g.b_bytes * g.n_kchunks + (AUX ? static_cast<uint32_t>(BN * g.aux_kb) : 0u));
                 for (int kc = 0; kc < g.n_kchunks; ++kc)
                     tma_load_2d(smem_u32(sB + kc * sb_stride), &map_b, bfull, kc * CB, nt * BN);
                 if (AUX) tma_load_2d(smem_u32(sBx), &map_xb, bfull, 0, nt * BN);
@@ -832,8 +845,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const uint64_t b_tap_step = static_cast<uint64_t>((g.n_cchunks * sb_stride) >> 4);
         const uint64_t a_stage_step = static_cast<uint64_t>(g.a_stage >> 4);
         const uint64_t b_chunk_step = static_cast<uint64_t>(sb_stride >> 4);
-        const uint64_t xadesc0 = AUX ? make_sdesc(smem_u32(sA + g.aux_off), 32) : 0;
-        const uint64_t xbdesc = AUX ? make_sdesc(smem_u32(sBx), 32) : 0;
+        const uint64_t xadesc0 = AUX ? make_sdesc(smem_u32(sA + g.aux_off), g.aux_kb) : 0;
+        const uint64_t xbdesc = AUX ? make_sdesc(smem_u32(sBx), g.aux_kb) : 0;
         bool ok = !g.b_resident || mbar_wait_warp(bfull, 0);
         if (!ok && lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
         int s = 0;
@@ -872,9 +885,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const uint64_t db = bdesc0 + static_cast<uint64_t>(g.b_resident ? ka : s) * b_chunk_step;
                     mma_chunk_elect<CB / 32>(d, da0, db, idesc, ka != 0 ? 1u : 0u);
                 }
-                if (AUX && ka == 0)
-                    mma_i8_elect(d + static_cast<uint32_t>(g.aux_col), xadesc0 + static_cast<uint64_t>(s) * a_stage_step,
-                                 xbdesc, idesc, 0u);
+                if (AUX && ka == 0) {
+                    const uint32_t dx = d + static_cast<uint32_t>(g.aux_col);
+                    const uint64_t xa = xadesc0 + static_cast<uint64_t>(s) * a_stage_step;
+                    if (g.aux_kb == 32) mma_chunk_elect<1>(dx, xa, xbdesc, idesc, 0u);
+                    else if (g.aux_kb == 64) mma_chunk_elect<2>(dx, xa, xbdesc, idesc, 0u);
+                    else mma_chunk_elect<4>(dx, xa, xbdesc, idesc, 0u);
+                }
                 mma_commit_elect(empty0 + 8 * s);
                 if (++s == S) { s = 0; ph ^= 1; }
             }
@@ -969,12 +986,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     if (valid) {
                         float y[16];
                         dequant16(v, fbr, e.act, y, !e.acc_small);
-                        if (AUX) dequant16(vx, afbr, e.aux_act, res, false);   // aux K = 32
+                        if (AUX) dequant16(vx, afbr, e.aux_act, res, false);   // aux K <= 128
                         finish16<RES, F32>(e, pf, ch, nv, y, res);
 #pragma unroll
                         for (int o = 0; o < 2; ++o) {
                             if (o >= n_out) continue;
-                            int8_t* qp = code_ptr(e, o, pq, n, ch);
+                            if (!code_kept(e, o, h, w)) continue;
+                            int8_t* qp = code_ptr(e, o, pq, n, ch, h, w);
                             if (nv == 16) {
                                 uint32_t w4[4];
                                 quant16q(y, o == 0 ? e.q0 : e.q1, o == 0 ? e.s0 : e.s1, lower, w4);
@@ -1035,7 +1053,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     if (!valid || nv <= 0) continue;
                     float y[16];
                     dequant16(v, cc.fb + ch, e.act, y, !e.acc_small);
-                    if (AUX) dequant16(vx, cc.aux_fb + ch, e.aux_act, res, false);   // aux K = 32
+                    if (AUX) dequant16(vx, cc.aux_fb + ch, e.aux_act, res, false);   // aux K <= 128
                     finish16<RES, F32>(e, pf, ch, nv, y, res);
                     // prefetch the next residual half of this warp
                     {
@@ -1054,7 +1072,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
                             for (int j = 0; j < 4; ++j) wq[o][hh * 4 + j] = w4[j];
                         } else {
-                            int8_t* qp = code_ptr(e, o, pq, n, ch);
+                            if (!code_kept(e, o, h, w)) continue;
+                            int8_t* qp = code_ptr(e, o, pq, n, ch, h, w);
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (j < nv) qp[j] = sat8(quant_code(y[j], inv, s));
@@ -1065,7 +1084,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 if (valid && nv32 == 32) {
 #pragma unroll
                     for (int o = 0; o < 2; ++o)
-                        if (o < n_out) st_v8(reinterpret_cast<uint32_t*>(code_ptr(e, o, pq, n, c0)), wq[o]);
+                        if (o < n_out && code_kept(e, o, h, w))
+                            st_v8(reinterpret_cast<uint32_t*>(code_ptr(e, o, pq, n, c0, h, w)), wq[o]);
                 }
             }
             tc_fence_before();

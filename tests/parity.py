@@ -31,6 +31,12 @@ def compare(engine, trace: O.Trace, model: O.Model, n: int, logits: np.ndarray, 
             ok = np.array_equal(got, exp)
         else:
             C = want.shape[1]
+            if got.shape[1:3] != want.shape[2:4]:
+                # a 1x1 stride-2 conv fused into its block's last conv keeps only the input
+                # codes it reads: the even positions
+                assert (conv.kh, conv.kw, conv.sh, conv.sw, conv.ph, conv.pw) == (1, 1, 2, 2, 0, 0), i
+                want = want[:, :, ::2, ::2]
+                assert got.shape[1:3] == want.shape[2:4], (i, got.shape, want.shape)
             ok = np.array_equal(got[..., :C], want.transpose(0, 2, 3, 1))
             if not ok:
                 d = got[..., :C].astype(np.int32) - want.transpose(0, 2, 3, 1)
