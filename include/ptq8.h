@@ -123,6 +123,10 @@ int ptq8_engine_set_input_shape(ptq8_engine* e, int c, int h, int w);
 int ptq8_engine_alloc_scratch(ptq8_engine* e, int max_batch);
 /* Int8Engine::set_stream - int8_engine.cuh:771 (NULL: engine-owned stream). */
 int ptq8_engine_set_stream(ptq8_engine* e, void* stream);
+/* Cap the persistent grid of every tensor-core conv at max_ctas CTAs (0: one per SM,
+ * the default) -- e.g. to leave SMs to other work.  No counterpart in the reference
+ * (its kernels are launched per tile).  Drops captured graphs. */
+int ptq8_engine_set_max_ctas(ptq8_engine* e, int max_ctas);
 void* ptq8_engine_stream(ptq8_engine* e);
 
 /* Int8Engine::forward(x_host, n, c, h, w, logits_host) - int8_engine.cuh:429-645.

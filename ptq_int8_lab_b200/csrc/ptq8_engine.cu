@@ -150,6 +150,7 @@ struct ptq8_engine {
     bool built = false, calibrated = false, planned = false;
     int in_c = 3, in_h = 32, in_w = 32;
     int max_batch = 0;
+    int max_ctas = 0;   // cap on the persistent grid of each tensor-core conv (0: all SMs)
     // plan
     std::vector<Value> vals;
     std::vector<Step> steps;
@@ -1042,7 +1043,8 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.stages = st.stages;
     g.b_resident = st.b_resident;
     g.b_bytes = (uint32_t)(st.bn * st.cb);
-    dim3 grid((unsigned)std::min(g.m_tiles, st.grid_x), (unsigned)st.n_ntiles);
+    const int gx = e->max_ctas > 0 ? std::min(st.grid_x, std::max(1, e->max_ctas / st.n_ntiles)) : st.grid_x;
+    dim3 grid((unsigned)std::min(g.m_tiles, gx), (unsigned)st.n_ntiles);
     CUtensorMap ma = st.map_a, mb = st.map_b, mxa = st.map_xa, mxb = st.map_xb;
     std::unique_ptr<ConvConsts> cc(new ConvConsts());   // zero past cout
     for (size_t c = 0; c < st.h_factor.size(); ++c) cc->fb[c] = make_float2(st.h_factor[c], st.h_bias[c]);
@@ -1530,6 +1532,14 @@ int ptq8_engine_set_input_shape(ptq8_engine* e, int c, int h, int w) {
 int ptq8_engine_alloc_scratch(ptq8_engine* e, int max_batch) {
     if (!e) return PTQ8_ERR_INVALID;
     return finalize(e, max_batch);
+}
+
+int ptq8_engine_set_max_ctas(ptq8_engine* e, int max_ctas) {
+    if (!e || max_ctas < 0) return PTQ8_ERR_INVALID;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);   // captured with the old grids
+    e->graphs.clear();
+    e->max_ctas = max_ctas;
+    return PTQ8_OK;
 }
 
 int ptq8_engine_set_stream(ptq8_engine* e, void* stream) {

@@ -40,7 +40,7 @@ EXPORTS = (
     "ptq8_quantize_device_noalloc",
     "ptq8_engine_create", "ptq8_engine_destroy", "ptq8_engine_last_error", "ptq8_engine_build",
     "ptq8_engine_set_act_mode", "ptq8_engine_set_calib", "ptq8_engine_set_input_shape",
-    "ptq8_engine_alloc_scratch", "ptq8_engine_set_stream", "ptq8_engine_stream", "ptq8_engine_forward",
+    "ptq8_engine_alloc_scratch", "ptq8_engine_set_stream", "ptq8_engine_set_max_ctas", "ptq8_engine_stream", "ptq8_engine_forward",
     "ptq8_engine_forward_device", "ptq8_engine_input_buffer", "ptq8_engine_logits_buffer", "ptq8_engine_run", "ptq8_engine_copy_logits",
     "ptq8_engine_sync", "ptq8_engine_check_device_error", "ptq8_engine_tensor_info", "ptq8_engine_dump",
     "ptq8_engine_n_launches", "ptq8_engine_passes_log", "ptq8_engine_profile",
@@ -98,6 +98,7 @@ def lib() -> ctypes.CDLL:
         "ptq8_engine_set_input_shape": (c_int, [c_void_p, c_int, c_int, c_int]),
         "ptq8_engine_alloc_scratch": (c_int, [c_void_p, c_int]),
         "ptq8_engine_set_stream": (c_int, [c_void_p, c_void_p]),
+        "ptq8_engine_set_max_ctas": (c_int, [c_void_p, c_int]),
         "ptq8_engine_stream": (c_void_p, [c_void_p]),
         "ptq8_engine_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
         "ptq8_engine_forward_device": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
@@ -281,6 +282,10 @@ class Int8Engine:
 
     def set_stream(self, stream_ptr: int):
         self._check(lib().ptq8_engine_set_stream(self._h, ctypes.c_void_p(stream_ptr)))
+
+    def set_max_ctas(self, max_ctas: int):
+        """Cap the persistent grid of every tensor-core conv (0: one CTA per SM)."""
+        self._check(lib().ptq8_engine_set_max_ctas(self._h, max_ctas))
 
     @property
     def stream(self) -> int:

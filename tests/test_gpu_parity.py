@@ -8,7 +8,7 @@ from tests.parity import compare
 pytestmark = pytest.mark.gpu
 
 
-def _run(paths, n, seed=7, passes=0, scale=1.0):
+def _run(paths, n, seed=7, passes=0, scale=1.0, max_ctas=0):
     from ptq_int8_lab_b200 import engine as E
     m = E.Model.load(paths["model"])
     ranges = E.load_ptqc(paths["calib"], m.n_conv)
@@ -17,6 +17,8 @@ def _run(paths, n, seed=7, passes=0, scale=1.0):
     eng.build(m, 8, 8, layer_bits=bits, passes=passes)
     eng.set_calib(ranges)
     eng.alloc_scratch(max(n, 8))
+    if max_ctas:
+        eng.set_max_ctas(max_ctas)
     x = (np.random.default_rng(seed).standard_normal((n, 3, 32, 32)) * scale).astype(np.float32)
     logits = eng.forward(x)
     om = O.read_model(paths["model"])
@@ -46,3 +48,21 @@ def test_ragged_batch(make_model):
     paths = make_model("resnet18", seed=0, bn="data")
     eng, tr, om, logits = _run(paths, 13, seed=3)
     compare(eng, tr, om, 13, logits)
+
+
+@pytest.mark.parametrize("key,kw", [("resnet18", dict(seed=0, bn="data")),
+                                    ("mobilenet_v2", dict(seed=2, bn="data", mixed=True))])
+def test_many_tiles_per_cta(make_model, key, kw):
+    """Three CTAs per conv: every CTA cycles through all accumulator buffers, barrier
+    phases and pipeline stages many times (a full-size batch does the same on 148 SMs)."""
+    paths = make_model(key, **kw)
+    eng, tr, om, logits = _run(paths, 13, seed=5, max_ctas=3)
+    compare(eng, tr, om, 13, logits)
+
+
+def test_batch_512_full_grid(make_model):
+    """Enough images that every CTA of the full persistent grid takes several tiles in the
+    64- and 128-channel convs."""
+    paths = make_model(0)
+    eng, tr, om, logits = _run(paths, 512, seed=9)
+    compare(eng, tr, om, 512, logits)
