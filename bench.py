@@ -31,6 +31,17 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "int8 images/sec ResNet-18 W8A8 32x32 at 1/2/4/8 B200; % of int8 TC/HBM roofline"
+METRIC_MV2 = "int8 images/sec MobileNetV2 32x32 (BASELINE configs 2/3) on B200; % of int8 TC/HBM roofline"
+
+
+def config_info(cfg: int) -> dict:
+    """Model, metric, default batch and workload name of BASELINE config `cfg`."""
+    from ptq_int8_lab_b200 import modelgen as mg
+    c = mg.CONFIGS[cfg]
+    mv2 = c["model"] == "mobilenet_v2"
+    prec = "w4w8a8_mixed" if c.get("mixed") else "w8a8"
+    return {"metric": METRIC_MV2 if mv2 else METRIC, "batch": c["batch"], "passes": 3 if c.get("passes") else 0,
+            "name": f"{'mobilenet_v2' if mv2 else 'resnet18_' + c['stem']}_{prec}"}
 
 
 def parse():
@@ -39,7 +50,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=8192, help="images per GPU")
+    ap.add_argument("--config", type=int, default=4, choices=range(5),
+                    help="BASELINE config (4: the headline ResNet-18 W8A8 at 8192 images per GPU)")
+    ap.add_argument("--batch", type=int, default=None, help="images per GPU (default: the config's batch)")
     ap.add_argument("--model-cache", default=os.environ.get("PTQ8_MODEL_CACHE", "/tmp/ptq8_models"))
     ap.add_argument("--cpu-sample", type=int, default=12, help="images in the timed CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -55,16 +68,21 @@ def dist_env():
 
 def model_files(cache: str, rank: int, world: int, barrier, cfg: int = 4):
     """Calibrated model files of BASELINE config `cfg` in `cache`: rank 0 writes them when
-    missing, every rank returns after the barrier."""
+    missing (with a marker naming them), every rank returns after the barrier."""
     from ptq_int8_lab_b200 import modelgen as mg
     d = Path(cache)
     d.mkdir(parents=True, exist_ok=True)
-    tag = "resnet18_cifar_s0"
-    paths = dict(model=d / f"{tag}.ptq2.bin", calib=d / f"calib_{tag}.ptqc", plan=d / f"layer_plan_{tag}.json")
-    if rank == 0 and not all(p.exists() for p in paths.values()):
-        mg.make_config(cfg, d)
+    marker = d / f"config{cfg}.json"
+    def ok():
+        if not marker.exists():
+            return False
+        p = json.loads(marker.read_text())
+        return all(Path(p[k]).exists() for k in ("model", "calib", "plan"))
+    if rank == 0 and not ok():
+        p = mg.make_config(cfg, d)
+        marker.write_text(json.dumps({k: str(p[k]) for k in ("model", "calib", "plan")}))
     barrier()
-    return {k: str(v) for k, v in paths.items()}
+    return json.loads(marker.read_text())
 
 
 def max_over_ranks(x: float, device) -> float:
@@ -158,10 +176,11 @@ def cpu_baseline(paths, n_img: int, seed: int = 99) -> dict:
     one core) on a bounded sample of the same workload, timed on this host."""
     import numpy as np
     from oracle import ptq8_oracle as O
+    from ptq_int8_lab_b200 import modelgen as mg
     O.MATMUL_MODE["mode"] = "int32"
     try:
         m = O.read_model(paths["model"])
-        orc = O.Oracle(m, O.read_ptqc(paths["calib"]))
+        orc = O.Oracle(m, O.read_ptqc(paths["calib"]), layer_bits=mg.read_layer_plan(paths["plan"]))
         x = np.random.default_rng(seed).standard_normal((n_img, 3, 32, 32)).astype(np.float32)
         orc.forward(x[:1], trace=False)
         t0 = time.perf_counter()
@@ -175,12 +194,13 @@ def cpu_baseline(paths, n_img: int, seed: int = 99) -> dict:
 
 
 def _ref_worker(args):
-    model, calib, n_img, seed = args
+    model, calib, plan, n_img, seed = args
     import numpy as np
     from oracle import ptq8_oracle as O
+    from ptq_int8_lab_b200 import modelgen as mg
     O.MATMUL_MODE["mode"] = "int32"
     m = O.read_model(model)
-    orc = O.Oracle(m, O.read_ptqc(calib))
+    orc = O.Oracle(m, O.read_ptqc(calib), layer_bits=mg.read_layer_plan(plan))
     x = np.random.default_rng(seed).standard_normal((n_img, 3, 32, 32)).astype(np.float32)
     t0 = time.perf_counter()
     orc.forward(x, trace=False)
@@ -193,25 +213,27 @@ def run_reference(a):
     if rank != 0:
         return
     import multiprocessing as mp
-    paths = model_files(a.model_cache, 0, 1, lambda: None)
+    info = config_info(a.config)
+    paths = model_files(a.model_cache, 0, 1, lambda: None, a.config)
     cores = os.cpu_count() or 1
     per = 2
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
         for _ in range(max(a.warmup, 1) if a.warmup else 0):
-            pool.map(_ref_worker, [(paths["model"], paths["calib"], 1, 7 + i) for i in range(cores)])
+            pool.map(_ref_worker, [(paths["model"], paths["calib"], paths["plan"], 1, 7 + i) for i in range(cores)])
         times = []
         for s in range(a.steps):
             t0 = time.perf_counter()
-            pool.map(_ref_worker, [(paths["model"], paths["calib"], per, 100 * s + i) for i in range(cores)])
+            pool.map(_ref_worker, [(paths["model"], paths["calib"], paths["plan"], per, 100 * s + i)
+                                   for i in range(cores)])
             times.append(time.perf_counter() - t0)
     imgs = per * cores * a.steps
     tot = sum(times)
     v = imgs / tot
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "images/s", "n_gpus": a.gpus,
+    line = {"impl": "reference", "metric": info["metric"], "value": v, "unit": "images/s", "n_gpus": a.gpus,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tot / a.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "resnet18_cifar_w8a8 (config 4 shapes)", "batch_per_step": per * cores,
+            "config": {"workload": f"{info['name']} (BASELINE configs[{a.config}] shapes)", "batch_per_step": per * cores,
                        "note": "bounded sample per step on host cores"},
             "cpu_baseline": {"value": v, "unit": "images/s", "cores": cores, "kind": "port",
                              "sample": f"{per} images per process x {cores} spawn processes per step, "
@@ -238,9 +260,11 @@ def main():
         barrier = lambda: dist.barrier()
     else:
         barrier = lambda: None
-    paths = model_files(a.model_cache, rank, world, barrier)
-    B = a.batch
-    eng = E.open_engine(paths["model"], paths["calib"], paths["plan"], max_batch=B, device=local)
+    info = config_info(a.config)
+    paths = model_files(a.model_cache, rank, world, barrier, a.config)
+    B = a.batch or info["batch"]
+    eng = E.open_engine(paths["model"], paths["calib"], paths["plan"], max_batch=B, device=local,
+                        passes=info["passes"])
     # a real (non-legacy) stream shared by the engine, torch events and NCCL
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -300,7 +324,7 @@ def main():
     # (captured at batch 2048 and scaled by 4; see the file); per forward like `achieved`
     traffic = None
     tp = ROOT / "profiles" / "conv_tc_traffic_resnet18_b8192.txt"
-    if tp.exists() and B == 8192:
+    if tp.exists() and a.config == 4 and B == 8192:
         for line in tp.read_text().splitlines():
             if line.startswith("traffic_bytes_per_forward_b8192 ="):
                 traffic = int(line.split("=")[1].strip())
@@ -329,10 +353,10 @@ def main():
            "h2d_bytes_per_step": B * 3 * 32 * 32 * 4, "d2h_bytes_per_step": B * 10 * 4}
 
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": a.steps,
+        line = {"metric": info["metric"], "value": value, "unit": "images/s", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-                "config": {"workload": "resnet18_cifar_w8a8_b8192 (BASELINE configs[4])", "batch_per_gpu": B,
+                "config": {"workload": f"{info['name']}_b{B} (BASELINE configs[{a.config}])", "batch_per_gpu": B,
                            "parallelism": f"dp{world}", "l2": "inputs and activations larger than L2 (>10 GB/step)",
                            "logits_gather": "nccl all_gather per step" if world > 1 else "none"},
                 "roofline": roofline, "e2e": e2e, "clocks": clk,
