@@ -20,6 +20,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <numeric>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -117,6 +118,13 @@ struct Step {
     int aux_off = 0;       // byte offset of the aux tile inside an A stage
     int acc_cols = 0;      // TMEM columns per accumulator buffer (main + aux)
     CUtensorMap map_xa{}, map_xb{};
+    // depthwise 3x3 / pad 1 / stride 1-2 (dw3x3_kernel): dp4a weight table, 3 uint4 per
+    // word of 4 channels; consumer threads (a multiple of 32 and of the word count), strip
+    // length T, unit shape (R output rows of one image, or k whole images), staged rows per
+    // image, stage bytes and count, CTAs of the persistent grid, kernel specialization
+    uint4* d_dwt = nullptr;
+    int dw_cons = 0, dw_T = 1, dw_R = 1, dw_kimg = 1, dw_rows = 0, dw_stage = 0, dw_stages = 2, dw_ctas = 1;
+    void* dw_kfn = nullptr;
 };
 
 struct ConvQ {   // quantized conv after graph passes
@@ -350,6 +358,81 @@ void choose_bn(int cout, int* bn, int* ntiles) {
 // channels (<= 128, so main + aux accumulators fit twice in TMEM), and the
 // block input is produced by a tensor-core conv (its epilogue writes the
 // subsampled codes the aux GEMM reads).
+// Depthwise convs that dw3x3_kernel runs: 3x3, padding 1, equal strides of 1 or 2,
+// codes out only (no residual, fp32 map or subsampled output), and a 4-channel word
+// count G4 with lcm(32, G4) <= 640 (the consumer threads are a multiple of both).
+bool dw3x3_eligible(const ptq8_engine* e, const Step& st) {
+    const int G4 = (st.oc + 3) / 4;
+    const Value& out = e->vals[st.out_val];
+    bool sub = false;
+    for (size_t k = 0; k < out.scales.size(); ++k) sub = sub || out.is_sub((int)k);
+    return st.kh == 3 && st.kw == 3 && st.ph == 1 && st.pw == 1 && st.sh == st.sw && (st.sh == 1 || st.sh == 2) &&
+           st.res_val < 0 && !out.need_f32 && !sub && st.act >= 0 && st.act <= 2 && !out.scales.empty() &&
+           out.scales.size() <= 2 && 32 / std::gcd(32, G4) * G4 <= kDwMaxConsumers;
+}
+
+// dw3x3_kernel specializations [T = 1, 2, 4][stride 1, 2][act 0, 1, 2]
+using DwKernel = void (*)(const int8_t*, const uint4*, const DwGeom, const EpiParams);
+template <int T, int S>
+constexpr DwKernel dw_k(int act) {
+    return act == 0 ? dw3x3_kernel<T, S, 0> : act == 1 ? dw3x3_kernel<T, S, 1> : dw3x3_kernel<T, S, 2>;
+}
+DwKernel dw_kernel_for(int T, int S, int act) {
+    if (T == 4) return S == 1 ? dw_k<4, 1>(act) : dw_k<4, 2>(act);
+    if (T == 2) return S == 1 ? dw_k<2, 1>(act) : dw_k<2, 2>(act);
+    return S == 1 ? dw_k<1, 1>(act) : dw_k<1, 2>(act);
+}
+
+// Strip length, unit shape, consumer count and pipeline depth of a dw3x3_kernel
+// launch (see the kernel).  Among consumer counts that are multiples of
+// lcm(32, G4) in [256, 640] and units whose staged bytes fit kDwStageMax, take the
+// best product of thread use (strips x words per unit over whole passes of the
+// consumers) and staged-row use (output rows x stride over staged rows); ties go to
+// more consumers, then to the larger unit.
+constexpr int kDwStageMax = 100 * 1024;
+constexpr int kDwSmemLimit = 210 * 1024;   // dynamic shared memory of any plan
+
+bool plan_dw3x3(const ptq8_engine* e, Step& st, int max_batch) {
+    const Value& vin = e->vals[st.in_val];
+    const int G4 = (st.oc + 3) / 4, S = st.sh;
+    st.dw_T = st.ow % 4 == 0 ? 4 : st.ow % 2 == 0 ? 2 : 1;
+    const long strips = st.ow / st.dw_T;
+    const long row = (long)(st.iw + 2) * vin.ldq;
+    const int l = 32 / std::gcd(32, G4) * G4;
+    std::vector<int> cons;
+    for (int b = l; b <= kDwMaxConsumers; b += l)
+        if (b >= 256 || b + l > kDwMaxConsumers) cons.push_back(b);
+    double best = -1.0;
+    auto consider = [&](int R, int k, int rows) {
+        const long bytes = (long)k * rows * row;
+        if (bytes > kDwStageMax) return;
+        const int stage = (int)((bytes + 127) / 128 * 128);
+        const int stages = std::min(kDwMaxStages, kDwSmemLimit / stage);
+        if (stages < 2) return;
+        const long items = (long)k * R * strips * G4;
+        const double rows_use = (double)(S * R) / rows;
+        for (int b : cons) {
+            const long passes = (items + b - 1) / b;
+            const double score = (double)items / (double)(passes * b) * rows_use + 1e-6 * b + 1e-9 * (double)items;
+            if (score > best) {
+                best = score;
+                st.dw_cons = b;
+                st.dw_R = R;
+                st.dw_kimg = k;
+                st.dw_rows = rows;
+                st.dw_stage = stage;
+                st.dw_stages = stages;
+            }
+        }
+    };
+    for (int R = 1; R <= st.oh; ++R)
+        if (st.oh % R == 0) consider(R, 1, S * (R - 1) + 3);
+    for (int k = 2; k <= std::max(2, max_batch) && (long)k * (st.ih + 2) * row <= kDwStageMax; ++k)
+        consider(st.oh, k, st.ih + 2);
+    st.dw_kfn = (void*)dw_kernel_for(st.dw_T, S, st.act);
+    return best > 0.0;
+}
+
 bool ds_fusable(const ptq8_engine* e, int ds, int ci, int in_val) {
     const ConvSpec& d = e->q[ds].spec;
     const ConvSpec& c = e->q[ci].spec;
@@ -706,6 +789,17 @@ int finalize(ptq8_engine* e, int max_batch) {
                 for (int t = 0; t < c.kh * c.kw; ++t) w[(size_t)t * c.cout + o] = cq.codes[(size_t)o * K + t];
             if (!e->dalloc(&st.d_w, w.size(), "alloc dw weights")) return PTQ8_ERR_CUDA;
             cudaMemcpy(st.d_w, w.data(), w.size(), cudaMemcpyHostToDevice);
+            if (dw3x3_eligible(e, st)) {
+                // word (j, c) of group g: column j of channel 4g + c, bytes (w[0][j], w[1][j], w[2][j], 0)
+                const int G4 = (c.cout + 3) / 4;
+                std::vector<uint32_t> t((size_t)G4 * 12, 0u);
+                auto code = [&](int o, int tap) { return (uint32_t)(uint8_t)cq.codes[(size_t)o * K + tap]; };
+                for (int o = 0; o < c.cout; ++o)
+                    for (int j = 0; j < 3; ++j)
+                        t[(size_t)(o / 4) * 12 + 4 * j + o % 4] = code(o, j) | code(o, 3 + j) << 8 | code(o, 6 + j) << 16;
+                if (!e->dalloc(&st.d_dwt, t.size() * 4, "alloc dw table")) return PTQ8_ERR_CUDA;
+                cudaMemcpy(st.d_dwt, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+            }
             continue;
         }
         // tensor-core conv: weight matrix [cout][ktot] int8, K-major
@@ -882,6 +976,22 @@ int finalize(ptq8_engine* e, int max_batch) {
             occ = std::max(1, std::min(occ, occ_tmem));
             st.grid_x = std::max(1, sms * occ / st.n_ntiles);
         }
+        // A kernel's shared-memory limit is a property of the function, shared by every
+        // engine of the process: always the same value, covering every plan.
+        for (Step& st : e->steps) {
+            if (st.kind != K_DW || !st.d_dwt) continue;
+            if (!plan_dw3x3(e, st, max_batch)) {
+                st.d_dwt = nullptr;   // no tiling fits: the generic depthwise kernel runs it
+                continue;
+            }
+            if (!e->cuda_ok(cudaFuncSetAttribute(st.dw_kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kDwSmemLimit),
+                            "dw smem attr"))
+                return PTQ8_ERR_CUDA;
+            int occ = 1;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, st.dw_kfn, st.dw_cons + 32,
+                                                          (size_t)st.dw_stages * st.dw_stage);
+            st.dw_ctas = std::max(1, occ) * sms;
+        }
     }
     if (!e->stream) {
         if (!e->cuda_ok(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) return PTQ8_ERR_CUDA;
@@ -970,6 +1080,33 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 32);
         launch_pdl(maxpool_kernel, dim3(grid), dim3(256), 0, s, e->vals[st.in_val].f32, n, st.ih, st.iw, st.ic, st.oh,
                    st.ow, ep);
+        return;
+    }
+    if (st.kind == K_DW && st.d_dwt) {
+        const Value& vin = e->vals[st.in_val];
+        DwGeom d{};
+        d.G4 = (st.oc + 3) / 4;
+        d.C = st.oc;
+        d.H = st.ih;
+        d.W = st.iw;
+        d.OH = st.oh;
+        d.OW = st.ow;
+        d.ldi = vin.ldq;
+        d.N = n;
+        d.R = st.dw_R;
+        d.k_img = st.dw_kimg;
+        d.rows_img = st.dw_rows;
+        d.bands = st.oh / st.dw_R;
+        d.n_units = st.dw_kimg > 1 ? (n + st.dw_kimg - 1) / st.dw_kimg : n * d.bands;
+        d.stage_bytes = st.dw_stage;
+        d.n_stages = st.dw_stages;
+        d.strips = st.ow / st.dw_T;
+        d.fd_strips = make_fastdiv(d.strips);
+        d.fd_rs = make_fastdiv(st.dw_R * d.strips);
+        d.fd_bands = make_fastdiv(d.bands);
+        const int grid = std::max(1, std::min(d.n_units, st.dw_ctas));
+        launch_pdl((DwKernel)st.dw_kfn, dim3(grid), dim3(st.dw_cons + 32), (size_t)d.n_stages * d.stage_bytes, s,
+                   vin.codes[vin.code_index(st.s_in)], (const uint4*)st.d_dwt, d, ep);
         return;
     }
     if (st.kind == K_DW) {

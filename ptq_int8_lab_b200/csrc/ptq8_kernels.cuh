@@ -1235,6 +1235,246 @@ __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int
     }
 }
 
+// Depthwise 3x3 conv, padding 1, stride S (1 or 2), over bordered int8 codes
+// [N][H+2][W+2][ldi]: the reference's depthwise conv (ref_int8.py conv with
+// groups == cin) for the 3x3 shapes MobileNetV2 uses.
+//
+// Staging: the input goes to shared memory by bulk copies (cp.async.bulk) in
+// n_stages stages, issued by one producer warp (the block's last) behind
+// full/empty mbarriers, so the copies run ahead of the arithmetic and consumer
+// warps never wait on one another.  A unit is either a band of R output rows of
+// one image (the S*(R-1)+3 bordered input rows it reads, contiguous in the
+// bordered layout) or k whole images (R = OH; all H+2 bordered rows of each).
+// Persistent CTAs take units blockIdx.x, +gridDim.x, ...
+//
+// Arithmetic: item = (strip of T horizontally adjacent output positions, word
+// g of 4 channels), item index strip * G4 + g: consecutive lanes read
+// consecutive 4-byte words of the same pixels.  The consumer count is a
+// multiple of G4, so a thread's g never changes and its weights (12 words) and
+// dequantization constants (4 pairs) stay in registers.  Weight word (j, c) of
+// the host table is column j of channel 4g+c's 3x3 kernel: bytes (w[0][j],
+// w[1][j], w[2][j], 0).  Each of the S*(T-1)+3 input columns of a strip is
+// loaded once (3 words: rows 0-2) and transposed with byte permutes into one
+// word per channel holding the column's 3 taps, which every position of the
+// strip that uses the column multiplies by the matching weight column with one
+// dp4a.  Integer sums are exact, so the order of taps does not change the
+// accumulator; |acc| <= 9 * 128 * 128 < 2^22 (float conversion without range
+// check).
+//
+// Epilogue: y = fadd(fmul(float(acc), factor), bias), then the activation and
+// the quantizer's clamp as one clamp: relu6 then clip to [y_lo, y_hi] is
+// clip(y, 0, min(6, y_hi)) (y_lo < 0), so codes are unchanged.  Channels c >= C
+// have zero weights and constants: their codes are 0, written into the code
+// row's padding (ldq >= 4 G4).  Convs with a residual, an fp32 output or a
+// subsampled code output use dw_conv_kernel.
+struct DwGeom {
+    int G4, C, H, W, OH, OW, ldi, N;
+    int R;            // output rows per unit
+    int k_img;        // images per unit (> 1 only when R == OH)
+    int rows_img;     // bordered input rows staged per image
+    int bands;        // OH / R
+    int n_units;
+    int stage_bytes;  // bytes per stage (multiple of 128)
+    int n_stages;
+    int strips;       // strips per output row (OW / T)
+    FastDiv fd_strips, fd_rs, fd_bands;   // strips, R * strips, bands
+};
+
+constexpr int kDwMaxStages = 4;
+constexpr int kDwMaxConsumers = 640;   // consumer threads per CTA (+ one producer warp)
+constexpr int kDwBulkChunk = 16384;    // bytes per bulk copy instruction
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// First image and first output row of unit u, and the byte range it stages.
+__device__ __forceinline__ void dw_unit(const DwGeom& d, int S, uint32_t u, int& n0, int& r0, int& k,
+                                        size_t& src_off, uint32_t& bytes) {
+    const size_t row = static_cast<size_t>(d.W + 2) * d.ldi;
+    if (d.k_img == 1) {
+        n0 = static_cast<int>(fdiv(u, d.fd_bands));
+        r0 = (static_cast<int>(u) - n0 * d.bands) * d.R;
+        k = 1;
+        src_off = (static_cast<size_t>(n0) * (d.H + 2) + static_cast<size_t>(r0) * S) * row;
+        bytes = static_cast<uint32_t>(d.rows_img * row);
+    } else {
+        n0 = static_cast<int>(u) * d.k_img;
+        r0 = 0;
+        k = min(d.k_img, d.N - n0);
+        src_off = static_cast<size_t>(n0) * (d.H + 2) * row;
+        bytes = static_cast<uint32_t>(k * (d.H + 2) * row);
+    }
+}
+
+// Column word x_i (row i, 4 channels) -> y[c] = (x0.b_c, x1.b_c, x2.b_c, *).
+// The fourth byte meets a zero weight byte.
+__device__ __forceinline__ void col_transpose3(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t (&y)[4]) {
+    const uint32_t a = __byte_perm(x0, x1, 0x5140);   // x0.b0 x1.b0 x0.b1 x1.b1
+    const uint32_t b = __byte_perm(x0, x1, 0x7362);   // x0.b2 x1.b2 x0.b3 x1.b3
+    y[0] = __byte_perm(a, x2, 0x5410);                // a.b0 a.b1 x2.b0 (x2.b1)
+    y[1] = __byte_perm(a, x2, 0x6532);                // a.b2 a.b3 x2.b1 (x2.b2)
+    y[2] = __byte_perm(b, x2, 0x7610);                // b.b0 b.b1 x2.b2 (x2.b3)
+    y[3] = __byte_perm(b, x2, 0x7732);                // b.b2 b.b3 x2.b3 (x2.b3)
+}
+
+template <int T, int S, int ACT>
+__global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const int8_t* __restrict__ in,
+                                                                        const uint4* __restrict__ wt, const DwGeom d,
+                                                                        const EpiParams e) {
+    extern __shared__ __align__(128) uint8_t dw_smem[];
+    __shared__ __align__(8) uint64_t bars[2 * kDwMaxStages];   // full[s], empty[s]
+    griddep_launch();
+    const int n_cons = static_cast<int>(blockDim.x) - 32;
+    const uint32_t bar0 = smem_u32(&bars[0]);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < d.n_stages; ++s) {
+            mbar_init(bar0 + 8 * s, 1);
+            mbar_init(bar0 + 8 * (kDwMaxStages + s), n_cons / 32);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (static_cast<int>(threadIdx.x) >= n_cons) {
+        // ---- producer warp
+        griddep_wait();
+        if (threadIdx.x != static_cast<unsigned>(n_cons)) return;
+        int issued = 0;
+        for (uint32_t u = blockIdx.x; u < static_cast<uint32_t>(d.n_units); u += gridDim.x, ++issued) {
+            const int stage = issued % d.n_stages;
+            if (issued >= d.n_stages &&
+                !mbar_wait(bar0 + 8 * (kDwMaxStages + stage), static_cast<uint32_t>(issued / d.n_stages - 1) & 1u)) {
+                atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
+                break;
+            }
+            int n0, r0, k;
+            size_t off;
+            uint32_t bytes;
+            dw_unit(d, S, u, n0, r0, k, off, bytes);
+            const uint32_t bar = bar0 + 8 * stage;
+            const uint32_t dst = smem_u32(dw_smem + stage * d.stage_bytes);
+            mbar_expect_tx(bar, bytes);
+            for (uint32_t b = 0; b < bytes; b += kDwBulkChunk)
+                bulk_load(dst + b, in + off + b, min(bytes - b, static_cast<uint32_t>(kDwBulkChunk)), bar);
+        }
+        // let the copies issued last land before the CTA's shared memory goes away
+        // (already complete unless a consumer gave up early)
+        for (int j = max(0, issued - d.n_stages); j < issued; ++j)
+            if (!mbar_wait(bar0 + 8 * (j % d.n_stages), static_cast<uint32_t>(j / d.n_stages) & 1u)) {
+                atomicExch(&g_ptq8_error, ERR_DRAIN);
+                break;
+            }
+        return;
+    }
+
+    // ---- consumers
+    const int G4 = d.G4;
+    const uint32_t g = threadIdx.x % static_cast<uint32_t>(G4);
+    const int c0 = 4 * static_cast<int>(g);
+    uint32_t w[12];   // w[3 j + ... ]: column j, channel c at w[4 j + c]
+    {
+        const uint4 a = __ldg(wt + 3 * g), b = __ldg(wt + 3 * g + 1), c = __ldg(wt + 3 * g + 2);
+        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+        w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+        w[8] = c.x; w[9] = c.y; w[10] = c.z; w[11] = c.w;
+    }
+    float2 fbc[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        fbc[c] = c0 + c < d.C ? make_float2(e.factor[c0 + c], e.bias[c0 + c]) : make_float2(0.0f, 0.0f);
+    // activation folded into the quantizer's clamp
+    QParams q0 = e.q0, q1 = e.q1;
+    if (ACT == 2) {
+        q0.y_hi = fminf(q0.y_hi, 6.0f);
+        q1.y_hi = fminf(q1.y_hi, 6.0f);
+    }
+    const int wp = d.W + 2;
+    const int ldi = d.ldi;
+    const int per_pass = n_cons / G4;   // strips per pass of the consumers
+    griddep_wait();
+
+    int it = 0;
+    for (uint32_t u = blockIdx.x; u < static_cast<uint32_t>(d.n_units); u += gridDim.x, ++it) {
+        const int stage = it % d.n_stages;
+        if (!mbar_wait_warp(bar0 + 8 * stage, static_cast<uint32_t>(it / d.n_stages) & 1u)) {
+            if ((threadIdx.x & 31) == 0) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+            break;
+        }
+        int n0, r0, k;
+        size_t off;
+        uint32_t bytes;
+        dw_unit(d, S, u, n0, r0, k, off, bytes);
+        const int nstrip = k * d.R * d.strips;
+        const uint8_t* sb = dw_smem + stage * d.stage_bytes + c0;
+        for (int sl = static_cast<int>(threadIdx.x) / G4; sl < nstrip; sl += per_pass) {
+            const int kk = static_cast<int>(fdiv(static_cast<uint32_t>(sl), d.fd_rs));
+            const int rem = sl - kk * d.R * d.strips;
+            const int rr = static_cast<int>(fdiv(static_cast<uint32_t>(rem), d.fd_strips));
+            const int cs = rem - rr * d.strips;
+            const uint8_t* base = sb + ((kk * d.rows_img + rr * S) * wp + cs * (T * S)) * ldi;
+            int acc[T][4];
+#pragma unroll
+            for (int t = 0; t < T; ++t)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[t][c] = 0;
+#pragma unroll
+            for (int j = 0; j < S * (T - 1) + 3; ++j) {
+                const uint8_t* col = base + j * ldi;
+                uint32_t y[4];
+                col_transpose3(*reinterpret_cast<const uint32_t*>(col),
+                               *reinterpret_cast<const uint32_t*>(col + wp * ldi),
+                               *reinterpret_cast<const uint32_t*>(col + 2 * wp * ldi), y);
+#pragma unroll
+                for (int t = 0; t < T; ++t) {
+                    const int jj = j - t * S;   // kernel column of this input column for position t
+                    if (jj >= 0 && jj < 3) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            acc[t][c] = __dp4a(static_cast<int>(y[c]), static_cast<int>(w[4 * jj + c]), acc[t][c]);
+                    }
+                }
+            }
+            // 16 values = T positions x 4 channels (T < 4: upper values unused)
+            uint32_t v[16];
+            float2 fb[16];
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    v[4 * t + c] = t < T ? static_cast<uint32_t>(acc[t < T ? t : 0][c]) : 0u;
+                    fb[4 * t + c] = fbc[c];
+                }
+            float y[16];
+            dequant16(v, fb, 0, y, false);
+            if (ACT != 0) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.0f);
+            }
+            const int n = n0 + kk, oh = r0 + rr, ow = cs * T;
+            const size_t pq = (static_cast<size_t>(n) * (d.OH + 2) + oh + 1) * (d.OW + 2) + ow + 1;
+            if (e.out_q0) {
+                uint32_t q[4];
+                quant16q(y, q0, e.s0, ACT == 0, q);
+                int8_t* o = e.out_q0 + pq * e.ldq0 + c0;
+#pragma unroll
+                for (int t = 0; t < T; ++t) *reinterpret_cast<uint32_t*>(o + t * e.ldq0) = q[t];
+            }
+            if (e.out_q1) {
+                uint32_t q[4];
+                quant16q(y, q1, e.s1, ACT == 0, q);
+                int8_t* o = e.out_q1 + pq * e.ldq1 + c0;
+#pragma unroll
+                for (int t = 0; t < T; ++t) *reinterpret_cast<uint32_t*>(o + t * e.ldq1) = q[t];
+            }
+        }
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(bar0 + 8 * (kDwMaxStages + stage));
+    }
+}
+
 // ------------------------------------------------------------------ stem maxpool
 
 // 3x3/s2/p1 maxpool (padding never wins) of an fp32 map [N][H][W][C]; writes the

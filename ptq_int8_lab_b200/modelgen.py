@@ -527,15 +527,18 @@ CONFIGS = {
 
 def build_calibrated(model_key: str, seed: int, stem: str = "cifar", mixed: bool = False,
                      out_dir=".", tag: Optional[str] = None, bn: str = "default",
-                     calib_n: int = CALIB_N) -> dict:
-    """Build, fold, calibrate, QDQ and export one synthetic calibrated model."""
+                     calib_n: int = CALIB_N, settings: Optional[Sequence] = None) -> dict:
+    """Build, fold, calibrate, QDQ and export one synthetic calibrated model.
+
+    ``settings``: MobileNetV2 stage table (t, c, n, s) in place of the CIFAR one
+    (e.g. expansion ratios whose depthwise channel counts are not multiples of 16)."""
     out = Path(out_dir)
     out.mkdir(parents=True, exist_ok=True)
     if model_key == "resnet18":
         m = build_resnet18(seed, stem)
         plan = resnet18_plan()
     elif model_key == "mobilenet_v2":
-        m = build_mobilenet_v2(seed)
+        m = build_mobilenet_v2(seed, settings=settings if settings is not None else MV2_SETTINGS_CIFAR)
         plan = mobilenet_v2_plan(m.settings)
     else:
         raise ValueError(model_key)
@@ -554,7 +557,8 @@ def build_calibrated(model_key: str, seed: int, stem: str = "cifar", mixed: bool
         bits = {n: 8 for n in names}
     qdq_weights(m, bits, fc_bits=8)
     tag = tag or (f"{model_key}_{stem if model_key == 'resnet18' else 'cifar'}_s{seed}"
-                  f"{'_mixed' if mixed else ''}{'' if bn == 'default' else '_bn' + bn}")
+                  f"{'_mixed' if mixed else ''}{'' if bn == 'default' else '_bn' + bn}"
+                  f"{'' if settings is None else '_st' + '_'.join('x'.join(map(str, r)) for r in settings)}")
     exp = export_ptq2(m, out / f"{tag}.ptq2.bin", plan, imgs[:2])
     pq = write_ptqc(out / f"calib_{tag}.ptqc", ranges)
     layers = [{"name": n, "bits": bits[n], "scheme": "per_channel"} for n in names]

@@ -66,3 +66,14 @@ def test_batch_512_full_grid(make_model):
     paths = make_model(0)
     eng, tr, om, logits = _run(paths, 512, seed=9)
     compare(eng, tr, om, 512, logits)
+
+
+RAGGED_MV2 = ((1, 16, 1, 1), (3, 40, 1, 2), (1, 40, 1, 1), (3, 24, 1, 2))
+
+
+def test_ragged_depthwise_channels(make_model):
+    """Depthwise convs of 32, 48, 40 and 120 channels at strides 1 and 2: the last group of 16
+    channels is partly padding in two of them (8 of 16 channels valid)."""
+    paths = make_model("mobilenet_v2", seed=4, bn="data", settings=RAGGED_MV2)
+    eng, tr, om, logits = _run(paths, 9, seed=13)
+    compare(eng, tr, om, 9, logits)
