@@ -123,6 +123,8 @@ struct Step {
     // length T, unit shape (R output rows of one image, or k whole images), staged rows per
     // image, stage bytes and count, CTAs of the persistent grid, kernel specialization
     uint4* d_dwt = nullptr;
+    // |acc| <= 128 * max_c sum_k |w[c][k]| < 2^22: accumulators convert to float without a range check
+    bool acc_small = false;
     int dw_cons = 0, dw_T = 1, dw_R = 1, dw_kimg = 1, dw_rows = 0, dw_stage = 0, dw_stages = 2, dw_ctas = 1;
     void* dw_kfn = nullptr;
 };
@@ -783,6 +785,15 @@ int finalize(ptq8_engine* e, int max_batch) {
         st.h_factor = factor;
         st.h_bias = cq.bias;
         const int K = c.cin * c.kh * c.kw;
+        {
+            long bound = 0;   // codes are in [-128, 127], so |acc| <= 128 * sum_k |w[c][k]|
+            for (int o = 0; o < c.cout; ++o) {
+                long sw = 0;
+                for (int k = 0; k < K; ++k) sw += std::abs((int)cq.codes[(size_t)o * K + k]);
+                bound = std::max(bound, 128 * sw);
+            }
+            st.acc_small = bound < (1L << 22);
+        }
         if (st.kind == K_DW) {
             std::vector<int8_t> w((size_t)c.kh * c.kw * c.cout);
             for (int o = 0; o < c.cout; ++o)
@@ -1018,10 +1029,7 @@ EpiParams epi_for(ptq8_engine* e, const Step& st) {
     }
     p.act = st.act;
     p.post = st.res_val >= 0 ? st.post : 0;
-    if (st.conv >= 0) {   // |acc| <= K * 128 * 128: below 2^22 for K < 256
-        const ConvSpec& c = e->q[st.conv].spec;
-        p.acc_small = c.in_channels() * c.kh * c.kw < 256 ? 1 : 0;
-    }
+    p.acc_small = st.acc_small ? 1 : 0;
     p.out_q0 = out.codes.size() > 0 ? out.codes[0] : nullptr;
     p.out_q1 = out.codes.size() > 1 ? out.codes[1] : nullptr;
     p.ldq0 = p.ldq1 = out.ldq;

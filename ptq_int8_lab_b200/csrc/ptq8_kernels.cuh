@@ -73,14 +73,19 @@ __device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
     asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// One try of a phase wait.  The suspend-time hint lets the hardware park the
+// thread until the phase completes (or the hint runs out) instead of returning at
+// once: spinning producer / MMA warps would otherwise take issue slots from the
+// epilogue warps of their SM sub-partitions.
+constexpr uint32_t kSuspendHintNs = 0x989680;   // 10 ms; the phase completing wakes the thread
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
@@ -341,10 +346,11 @@ __device__ __forceinline__ int quant_exact(float y, double s) {
 
 // Two-lane float add with one IEEE rounding per lane (add.rn.f32x2).
 //
-// The dequantization's multiply and add stay scalar (__fmul_rn, __fadd_rn):
-// written as mul.rn.f32x2 followed by add.rn.f32x2, on sm_100a with CUDA 12.9,
-// the pair gave results one ulp away from two separate roundings, as a fused
-// multiply-add would.
+// The dequantization's multiply and add stay scalar (__fmul_rn, __fadd_rn): on
+// sm_100a with CUDA 12.9, the packed pair -- written as inline-asm mul.rn.f32x2
+// followed by add.rn.f32x2, and again as the __fmul2_rn / __fadd2_rn intrinsics --
+// gave codes one step away from the two separate roundings in a few values per
+// million, as a fused multiply-add would.
 __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
     float2 r;
     asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
@@ -392,9 +398,9 @@ __device__ __noinline__ void quant16_exact(const float* y, double s, uint32_t* w
 // [k-1/2, k+1/2]; double(y)/s lies strictly inside that interval with a gap far
 // larger than its float64 rounding, so it rounds (half away) to k as well.
 // Otherwise a half-integer lies in between and the float64 formula decides for
-// the 16 values.  `lower`: y may lie below y_lo (false when y >= 0 is known).
-__device__ __forceinline__ void quant16q(const float (&y)[16], const QParams& q, double s, bool lower,
-                                         uint32_t (&w)[4]) {
+// the 16 values.  LOWER: y may lie below y_lo (false when y >= 0 is known).
+template <bool LOWER>
+__device__ __forceinline__ void quant16q(const float (&y)[16], const QParams& q, double s, uint32_t (&w)[4]) {
     const float2 lo2 = make_float2(q.inv_lo, q.inv_lo);
     const float2 hi2 = make_float2(q.inv_hi, q.inv_hi);
     const float2 mg = make_float2(kRoundMagic, kRoundMagic);
@@ -402,7 +408,7 @@ __device__ __forceinline__ void quant16q(const float (&y)[16], const QParams& q,
 #pragma unroll
     for (int j = 0; j < 16; j += 2) {
         float c0 = fminf(y[j], q.y_hi), c1 = fminf(y[j + 1], q.y_hi);
-        if (lower) {
+        if (LOWER) {
             c0 = fmaxf(c0, q.y_lo);
             c1 = fmaxf(c1, q.y_lo);
         }
@@ -419,14 +425,34 @@ __device__ __forceinline__ void quant16q(const float (&y)[16], const QParams& q,
         w[k] = __byte_perm(__byte_perm(m[4 * k], m[4 * k + 1], 0x0040), __byte_perm(m[4 * k + 2], m[4 * k + 3], 0x0040),
                            0x5410);
     if (flag) {
+        // the same clamp first: it may carry a folded activation (fold_act)
         float ys[16];
         uint32_t ws[4];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ys[j] = y[j];
+        for (int j = 0; j < 16; ++j) ys[j] = LOWER ? fmaxf(fminf(y[j], q.y_hi), q.y_lo) : fminf(y[j], q.y_hi);
         quant16_exact(ys, s, ws);
 #pragma unroll
         for (int j = 0; j < 4; ++j) w[j] = ws[j];
     }
+}
+
+// quant16q with `lower` known only at run time (a warp-uniform branch, no
+// predicated clamps).
+__device__ __forceinline__ void quant16q_rt(const float (&y)[16], const QParams& q, double s, bool lower,
+                                            uint32_t (&w)[4]) {
+    if (lower)
+        quant16q<true>(y, q, s, w);
+    else
+        quant16q<false>(y, q, s, w);
+}
+
+// QParams whose clamp also applies the activation of a conv whose fp32 values are
+// not kept: relu then clip to [y_lo, y_hi] is clip(y, 0, y_hi), relu6 is
+// clip(y, 0, min(6, y_hi)) (y_lo < 0 < y_hi), so the codes are unchanged.
+__device__ __forceinline__ QParams fold_act(QParams q, int act) {
+    if (act != 0) q.y_lo = 0.0f;
+    if (act == 2) q.y_hi = fminf(q.y_hi, 6.0f);
+    return q;
 }
 
 __device__ __forceinline__ int quant_code(float x, float inv, double s) {
@@ -494,7 +520,7 @@ struct EpiParams {
     // (sub_h+2) x (sub_w+2) map at (h/2, w/2) -- the input of a fused 1x1 stride-2 conv
     int sub_mask;
     int sub_h, sub_w;
-    int acc_small; // 1 when K * 128 * 128 < 2^22: accumulators convert to float without a range check
+    int acc_small; // 1 when 128 * sum_k |w[c][k]| < 2^22 for every c: no range check in the float conversion
     int post;   // residual: 0 none, 1 add then relu, 2 add only
     // positional decomposition: channel c' = pos*dcr_oc + c of a 1x1 GEMM output is code
     // (pos / dcr_w, pos % dcr_w, c) of a dcr_h x dcr_w map (DepthToSpace, DCR order)
@@ -550,7 +576,7 @@ __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0
 // |acc| < 2^22 (exact subtraction afterwards); in that range the pattern xor
 // 0x4B000000 stays below 2^23, so one OR over the 16 patterns tells whether
 // every accumulator was in range.  Otherwise the rounding conversion is used.
-// `check` false: the caller knows |acc| < 2^22 (K * 128 * 128 < 2^22, i.e. K < 256).
+// `check` false: the caller knows |acc| < 2^22 (128 * sum |w| < 2^22 for every channel).
 __device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float2* fb, int act, float (&y)[16],
                                           bool check = true) {
     uint32_t range = 0;
@@ -921,6 +947,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         constexpr int n_out = NOUT;
         // codes can only saturate low when the values are not already clipped at zero
         const bool lower = RES ? e.post != 1 : e.act == 0;
+        // codes only (no fp32 values kept): the activation is folded into the quantizer's clamp
+        constexpr bool kFold = !RES && !F32 && !AUX;
+        const QParams qf0 = fold_act(e.q0, e.act), qf1 = fold_act(e.q1, e.act);
         griddep_wait();   // residuals are earlier kernels' outputs
         // output position of this thread's row r in M tile mt: image n, row h, column w,
         // bordered code row pq, fp32 row pf
@@ -995,7 +1024,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             int8_t* qp = code_ptr(e, o, pq, n, ch, h, w);
                             if (nv == 16) {
                                 uint32_t w4[4];
-                                quant16q(y, o == 0 ? e.q0 : e.q1, o == 0 ? e.s0 : e.s1, lower, w4);
+                                quant16q_rt(y, o == 0 ? e.q0 : e.q1, o == 0 ? e.s0 : e.s1, lower, w4);
                                 *reinterpret_cast<uint4*>(qp) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                             } else {
                                 const float inv = o == 0 ? e.inv0 : e.inv1;
@@ -1052,7 +1081,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const int nv = min(16, tile_end - ch);
                     if (!valid || nv <= 0) continue;
                     float y[16];
-                    dequant16(v, cc.fb + ch, e.act, y, !e.acc_small);
+                    dequant16(v, cc.fb + ch, kFold ? 0 : e.act, y, !e.acc_small);
                     if (AUX) dequant16(vx, cc.aux_fb + ch, e.aux_act, res, false);   // aux K <= 128
                     finish16<RES, F32>(e, pf, ch, nv, y, res);
                     // prefetch the next residual half of this warp
@@ -1068,7 +1097,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         const double s = o == 0 ? e.s0 : e.s1;
                         if (nv32 == 32) {
                             uint32_t w4[4];
-                            quant16q(y, o == 0 ? e.q0 : e.q1, s, lower, w4);
+                            if (kFold)
+                                quant16q<true>(y, o == 0 ? qf0 : qf1, s, w4);
+                            else
+                                quant16q_rt(y, o == 0 ? e.q0 : e.q1, s, lower, w4);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) wq[o][hh * 4 + j] = w4[j];
                         } else {
@@ -1076,7 +1108,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             int8_t* qp = code_ptr(e, o, pq, n, ch, h, w);
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
-                                if (j < nv) qp[j] = sat8(quant_code(y[j], inv, s));
+                                if (j < nv) qp[j] = sat8(quant_code(kFold ? apply_act(y[j], e.act) : y[j], inv, s));
                         }
                     }
                 }
@@ -1457,14 +1489,14 @@ __global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const in
             const size_t pq = (static_cast<size_t>(n) * (d.OH + 2) + oh + 1) * (d.OW + 2) + ow + 1;
             if (e.out_q0) {
                 uint32_t q[4];
-                quant16q(y, q0, e.s0, ACT == 0, q);
+                quant16q<ACT == 0>(y, q0, e.s0, q);
                 int8_t* o = e.out_q0 + pq * e.ldq0 + c0;
 #pragma unroll
                 for (int t = 0; t < T; ++t) *reinterpret_cast<uint32_t*>(o + t * e.ldq0) = q[t];
             }
             if (e.out_q1) {
                 uint32_t q[4];
-                quant16q(y, q1, e.s1, ACT == 0, q);
+                quant16q<ACT == 0>(y, q1, e.s1, q);
                 int8_t* o = e.out_q1 + pq * e.ldq1 + c0;
 #pragma unroll
                 for (int t = 0; t < T; ++t) *reinterpret_cast<uint32_t*>(o + t * e.ldq1) = q[t];
@@ -1523,7 +1555,7 @@ __global__ void quantize_kernel(const float* __restrict__ x, size_t n, QParams q
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] = x[base + j];
         uint32_t w[4];
-        quant16q(y, q, s, true, w);
+        quant16q<true>(y, q, s, w);
 #pragma unroll
         for (int j = 0; j < 4; ++j) reinterpret_cast<uint32_t*>(out + base)[j] = w[j];
     } else {
