@@ -73,19 +73,16 @@ __device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
     asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// One try of a phase wait.  The suspend-time hint lets the hardware park the
-// thread until the phase completes (or the hint runs out) instead of returning at
-// once: spinning producer / MMA warps would otherwise take issue slots from the
-// epilogue warps of their SM sub-partitions.
-constexpr uint32_t kSuspendHintNs = 0x989680;   // 10 ms; the phase completing wakes the thread
+// One try of a phase wait.  (A suspend-time hint here, and a nanosleep back-off in
+// mbar_wait, were both measured: neither changed a conv's time.)
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+        : "r"(bar), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -436,16 +433,6 @@ __device__ __forceinline__ void quant16q(const float (&y)[16], const QParams& q,
     }
 }
 
-// quant16q with `lower` known only at run time (a warp-uniform branch, no
-// predicated clamps).
-__device__ __forceinline__ void quant16q_rt(const float (&y)[16], const QParams& q, double s, bool lower,
-                                            uint32_t (&w)[4]) {
-    if (lower)
-        quant16q<true>(y, q, s, w);
-    else
-        quant16q<false>(y, q, s, w);
-}
-
 // QParams whose clamp also applies the activation of a conv whose fp32 values are
 // not kept: relu then clip to [y_lo, y_hi] is clip(y, 0, y_hi), relu6 is
 // clip(y, 0, min(6, y_hi)) (y_lo < 0 < y_hi), so the codes are unchanged.
@@ -613,7 +600,9 @@ __device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float2*
 }
 
 // Residual add + post activation and the fp32 store of 16 channels [c0, c0+16) (nv valid).
-template <bool RES, bool F32>
+// POST_RELU false: the caller folds the post-add ReLU into the quantizer's clamp
+// (no fp32 values are stored).
+template <bool RES, bool F32, bool POST_RELU = true>
 __device__ __forceinline__ void finish16(const EpiParams& e, size_t pf, int c0, int nv, float (&y)[16],
                                          const float (&r)[16]) {
     if constexpr (RES) {
@@ -623,7 +612,7 @@ __device__ __forceinline__ void finish16(const EpiParams& e, size_t pf, int c0, 
             y[j] = t.x;
             y[j + 1] = t.y;
         }
-        if (e.post == 1) {
+        if (POST_RELU && e.post == 1) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.0f);
         }
@@ -945,11 +934,27 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const int tile_end = min(e.cout, (nt + 1) * BN);
         const int ncg = bn32 / 32;   // 32-column groups, each handled as two 16-column halves
         constexpr int n_out = NOUT;
-        // codes can only saturate low when the values are not already clipped at zero
-        const bool lower = RES ? e.post != 1 : e.act == 0;
-        // codes only (no fp32 values kept): the activation is folded into the quantizer's clamp
-        constexpr bool kFold = !RES && !F32 && !AUX;
-        const QParams qf0 = fold_act(e.q0, e.act), qf1 = fold_act(e.q1, e.act);
+        // One quantizer form (clamp to [y_lo, y_hi]) for every output.  Codes only (no fp32
+        // values kept): the conv's activation (no residual) or the post-add ReLU (residual)
+        // is folded into that clamp.  With fp32 values kept, the values are final and the
+        // lower bound is 0 where they cannot be negative (the clamp then changes nothing).
+        constexpr bool kFold = !RES && !F32 && !AUX;      // activation folded
+        constexpr bool kFoldPost = RES && !F32;           // post-add ReLU folded
+        const bool nonneg = RES ? e.post == 1 : e.act != 0;
+        QParams qx0 = e.q0, qx1 = e.q1;
+        if (kFold) {
+            qx0 = fold_act(e.q0, e.act);
+            qx1 = fold_act(e.q1, e.act);
+        } else if (nonneg) {
+            qx0.y_lo = 0.0f;
+            qx1.y_lo = 0.0f;
+        }
+        // the value a code encodes, for the per-value path of partial channel groups
+        auto final_val = [&](float v) {
+            if (kFold) return apply_act(v, e.act);
+            if (kFoldPost && e.post == 1) return fmaxf(v, 0.0f);
+            return v;
+        };
         griddep_wait();   // residuals are earlier kernels' outputs
         // output position of this thread's row r in M tile mt: image n, row h, column w,
         // bordered code row pq, fp32 row pf
@@ -1016,7 +1021,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         float y[16];
                         dequant16(v, fbr, e.act, y, !e.acc_small);
                         if (AUX) dequant16(vx, afbr, e.aux_act, res, false);   // aux K <= 128
-                        finish16<RES, F32>(e, pf, ch, nv, y, res);
+                        finish16<RES, F32, !kFoldPost>(e, pf, ch, nv, y, res);
 #pragma unroll
                         for (int o = 0; o < 2; ++o) {
                             if (o >= n_out) continue;
@@ -1024,14 +1029,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             int8_t* qp = code_ptr(e, o, pq, n, ch, h, w);
                             if (nv == 16) {
                                 uint32_t w4[4];
-                                quant16q_rt(y, o == 0 ? e.q0 : e.q1, o == 0 ? e.s0 : e.s1, lower, w4);
+                                quant16q<true>(y, o == 0 ? qx0 : qx1, o == 0 ? e.s0 : e.s1, w4);
                                 *reinterpret_cast<uint4*>(qp) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                             } else {
                                 const float inv = o == 0 ? e.inv0 : e.inv1;
                                 const double s = o == 0 ? e.s0 : e.s1;
 #pragma unroll
                                 for (int j = 0; j < 16; ++j)
-                                    if (j < nv) qp[j] = sat8(quant_code(y[j], inv, s));
+                                    if (j < nv) qp[j] = sat8(quant_code(final_val(y[j]), inv, s));
                             }
                         }
                     }
@@ -1083,7 +1088,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     float y[16];
                     dequant16(v, cc.fb + ch, kFold ? 0 : e.act, y, !e.acc_small);
                     if (AUX) dequant16(vx, cc.aux_fb + ch, e.aux_act, res, false);   // aux K <= 128
-                    finish16<RES, F32>(e, pf, ch, nv, y, res);
+                    finish16<RES, F32, !kFoldPost>(e, pf, ch, nv, y, res);
                     // prefetch the next residual half of this warp
                     {
                         const int cn = hh == 0 ? ch + 16 : c0 + 32 * kSlices;
@@ -1097,10 +1102,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         const double s = o == 0 ? e.s0 : e.s1;
                         if (nv32 == 32) {
                             uint32_t w4[4];
-                            if (kFold)
-                                quant16q<true>(y, o == 0 ? qf0 : qf1, s, w4);
-                            else
-                                quant16q_rt(y, o == 0 ? e.q0 : e.q1, s, lower, w4);
+                            quant16q<true>(y, o == 0 ? qx0 : qx1, s, w4);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) wq[o][hh * 4 + j] = w4[j];
                         } else {
@@ -1108,7 +1110,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             int8_t* qp = code_ptr(e, o, pq, n, ch, h, w);
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
-                                if (j < nv) qp[j] = sat8(quant_code(kFold ? apply_act(y[j], e.act) : y[j], inv, s));
+                                if (j < nv) qp[j] = sat8(quant_code(final_val(y[j]), inv, s));
                         }
                     }
                 }
