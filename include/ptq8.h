@@ -132,6 +132,14 @@ void* ptq8_engine_stream(ptq8_engine* e);
 /* Int8Engine::forward(x_host, n, c, h, w, logits_host) - int8_engine.cuh:429-645.
  * Host buffers: H2D, the whole forward as one CUDA graph, D2H, synchronize. */
 int ptq8_engine_forward(ptq8_engine* e, const float* x_host, int n, int c, int h, int w, float* logits_host);
+/* Pipelined host-buffer forward (no counterpart in the reference, whose forward is
+ * synchronous): enqueues the H2D copy of x_host into one of two engine input slots on
+ * an engine-owned copy stream, the forward (CUDA graph) on the engine stream once that
+ * copy has landed, and the D2H copy of the logits; returns without waiting.  The H2D of
+ * call k+1 overlaps the forward of call k.  ptq8_engine_sync() waits for every enqueued
+ * call.  x_host (pinned, for the copies to overlap) must stay unchanged and logits_host
+ * unread until then.  Same logits as ptq8_engine_forward. */
+int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float* logits_host);
 /* Device-pointer forward (fp32 NCHW input, fp32 [n][fc_out] logits); enqueued
  * on the engine stream, not synchronized. */
 int ptq8_engine_forward_device(ptq8_engine* e, const float* x_dev, int n, float* logits_dev);

@@ -167,6 +167,13 @@ struct ptq8_engine {
     int final_val = -1;
     std::vector<int> conv_step;    // conv index -> step index
     float* d_input = nullptr;      // fp32 NCHW [max_batch][3][32][32]
+    // pipelined host-buffer forward (ptq8_engine_forward_async): second input slot,
+    // copy stream, per-slot events, next slot; graphs are keyed by batch * 2 + slot
+    float* d_input2 = nullptr;
+    const float* cur_input = nullptr;   // the input the stem reads while a forward is enqueued
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_staged[2] = {nullptr, nullptr}, ev_free[2] = {nullptr, nullptr};
+    int async_slot = 0;
     float* d_logits = nullptr;
     float* d_fc_w = nullptr;
     float* d_fc_b = nullptr;
@@ -177,10 +184,19 @@ struct ptq8_engine {
     ~ptq8_engine() { release(); }
 
     void release() {
+        if (copy_stream) cudaStreamSynchronize(copy_stream);
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         graphs.clear();
         for (void* p : allocs) cudaFree(p);
         allocs.clear();
+        d_input2 = nullptr;
+        for (int k = 0; k < 2; ++k) {
+            if (ev_staged[k]) cudaEventDestroy(ev_staged[k]);
+            if (ev_free[k]) cudaEventDestroy(ev_free[k]);
+            ev_staged[k] = ev_free[k] = nullptr;
+        }
+        if (copy_stream) cudaStreamDestroy(copy_stream);
+        copy_stream = nullptr;
         if (own_stream && stream) cudaStreamDestroy(stream);
         stream = nullptr;
         own_stream = false;
@@ -731,10 +747,13 @@ int finalize(ptq8_engine* e, int max_batch) {
     if (!e->calibrated) return e->fail("calibration ranges not set (set_calib)");
     if (max_batch <= 0) return e->fail("max_batch must be positive");
     if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
+    if (e->copy_stream) cudaStreamSynchronize(e->copy_stream);
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
     for (void* p : e->allocs) cudaFree(p);
     e->allocs.clear();
+    e->d_input2 = nullptr;
+    e->async_slot = 0;
     e->planned = false;
     int rc = plan(e);
     if (rc) return rc;
@@ -1135,7 +1154,8 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         const int bands = (st.oh + rows - 1) / rows;
         const size_t band_bytes =
             (((size_t)c.cin * ((rows - 1) * c.sh + c.kh) * band_w + 15) & ~(size_t)15) + (size_t)st.kpad * sizeof(int);
-        launch_pdl(stem_im2col_kernel, dim3(n * bands), dim3(256), band_bytes, s, (const float*)e->d_input,
+        launch_pdl(stem_im2col_kernel, dim3(n * bands), dim3(256), band_bytes, s,
+                   e->cur_input ? e->cur_input : (const float*)e->d_input,
                    st.d_im2col, n, c.cin, st.ih, st.iw, st.oh, st.ow, c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad, rows,
                    (float)(1.0 / st.s_in), st.s_in);
     }
@@ -1261,8 +1281,9 @@ void step_work(const ptq8_engine* e, int n, size_t si, double* macs, double* byt
     }
 }
 
-// The CUDA graph of one forward at batch n (captured on first use, then cached).
-int graph_for(ptq8_engine* e, int n, cudaGraphExec_t* out) {
+// The CUDA graph of one forward at batch n reading input slot `slot` (0: d_input,
+// 1: d_input2), captured on first use, then cached.
+int graph_for(ptq8_engine* e, int n, cudaGraphExec_t* out, int slot = 0) {
     if (!e->planned) {
         int rc = finalize(e, std::max(n, e->max_batch > 0 ? e->max_batch : n));
         if (rc) return rc;
@@ -1270,12 +1291,15 @@ int graph_for(ptq8_engine* e, int n, cudaGraphExec_t* out) {
     if (n <= 0 || n > e->max_batch)
         return e->fail(strf("batch %d outside [1, %d] (alloc_scratch sets the maximum)", n, e->max_batch));
     if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
-    auto it = e->graphs.find(n);
+    const int key = n * 2 + slot;
+    auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         cudaGraph_t g;
         if (!e->cuda_ok(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture"))
             return PTQ8_ERR_CUDA;
+        e->cur_input = slot ? e->d_input2 : e->d_input;
         int rc = enqueue(e, n);
+        e->cur_input = nullptr;
         cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
         if (rc) return rc;
         if (!e->cuda_ok(ce, "end capture")) return PTQ8_ERR_CUDA;
@@ -1283,7 +1307,7 @@ int graph_for(ptq8_engine* e, int n, cudaGraphExec_t* out) {
         ce = cudaGraphInstantiate(&ge, g, 0);
         cudaGraphDestroy(g);
         if (!e->cuda_ok(ce, "graph instantiate")) return PTQ8_ERR_CUDA;
-        it = e->graphs.emplace(n, ge).first;
+        it = e->graphs.emplace(key, ge).first;
     }
     *out = it->second;
     return PTQ8_OK;
@@ -1718,6 +1742,7 @@ int ptq8_engine_forward_device(ptq8_engine* e, const float* x_dev, int n, float*
         if (rc) return rc;
     }
     if (n <= 0 || n > e->max_batch) return e->fail(strf("batch %d outside [1, %d]", n, e->max_batch));
+    if (e->copy_stream && !e->cuda_ok(cudaStreamSynchronize(e->copy_stream), "copy stream")) return PTQ8_ERR_CUDA;
     const size_t in_bytes = (size_t)n * e->in_c * e->in_h * e->in_w * sizeof(float);
     if (x_dev != e->d_input &&
         !e->cuda_ok(cudaMemcpyAsync(e->d_input, x_dev, in_bytes, cudaMemcpyDeviceToDevice, e->stream), "input copy"))
@@ -1741,6 +1766,8 @@ int ptq8_engine_forward(ptq8_engine* e, const float* x_host, int n, int c, int h
         if (rc) return rc;
     }
     if (n <= 0 || n > e->max_batch) return e->fail(strf("batch %d outside [1, %d]", n, e->max_batch));
+    // a pipelined call's copy into the same input slot may still be in flight
+    if (e->copy_stream && !e->cuda_ok(cudaStreamSynchronize(e->copy_stream), "copy stream")) return PTQ8_ERR_CUDA;
     const size_t in_bytes = (size_t)n * c * h * w * sizeof(float);
     if (!e->cuda_ok(cudaMemcpyAsync(e->d_input, x_host, in_bytes, cudaMemcpyHostToDevice, e->stream), "H2D"))
         return PTQ8_ERR_CUDA;
@@ -1752,6 +1779,52 @@ int ptq8_engine_forward(ptq8_engine* e, const float* x_host, int n, int c, int h
         return PTQ8_ERR_CUDA;
     if (!e->cuda_ok(cudaStreamSynchronize(e->stream), "forward")) return PTQ8_ERR_CUDA;
     return ptq8_engine_check_device_error(e);
+}
+
+int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float* logits_host) {
+    try {
+        if (!e || !x_host || !logits_host) return PTQ8_ERR_INVALID;
+        if (!e->planned) {
+            int rc = finalize(e, std::max(n, e->max_batch));
+            if (rc) return rc;
+        }
+        if (n <= 0 || n > e->max_batch) return e->fail(strf("batch %d outside [1, %d]", n, e->max_batch));
+        if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
+        const size_t in_bytes = (size_t)n * e->in_c * e->in_h * e->in_w * sizeof(float);
+        if (!e->copy_stream) {
+            if (!e->cuda_ok(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking), "copy stream"))
+                return PTQ8_ERR_CUDA;
+            for (int k = 0; k < 2; ++k)
+                if (!e->cuda_ok(cudaEventCreateWithFlags(&e->ev_staged[k], cudaEventDisableTiming), "event") ||
+                    !e->cuda_ok(cudaEventCreateWithFlags(&e->ev_free[k], cudaEventDisableTiming), "event"))
+                    return PTQ8_ERR_CUDA;
+        }
+        if (!e->d_input2 &&
+            !e->dalloc(&e->d_input2, (size_t)e->max_batch * e->in_c * e->in_h * e->in_w * sizeof(float),
+                       "alloc second input slot"))
+            return PTQ8_ERR_CUDA;
+        const int slot = e->async_slot;
+        float* dst = slot ? e->d_input2 : e->d_input;
+        cudaGraphExec_t ge;
+        int rc = graph_for(e, n, &ge, slot);
+        if (rc) return rc;
+        // the slot is free once the forward that last read it has run (a never-recorded
+        // event is no dependency)
+        if (!e->cuda_ok(cudaStreamWaitEvent(e->copy_stream, e->ev_free[slot], 0), "wait slot") ||
+            !e->cuda_ok(cudaMemcpyAsync(dst, x_host, in_bytes, cudaMemcpyHostToDevice, e->copy_stream), "H2D") ||
+            !e->cuda_ok(cudaEventRecord(e->ev_staged[slot], e->copy_stream), "record staged") ||
+            !e->cuda_ok(cudaStreamWaitEvent(e->stream, e->ev_staged[slot], 0), "wait staged") ||
+            !e->cuda_ok(cudaGraphLaunch(ge, e->stream), "graph launch") ||
+            !e->cuda_ok(cudaEventRecord(e->ev_free[slot], e->stream), "record free") ||
+            !e->cuda_ok(cudaMemcpyAsync(logits_host, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
+                                        cudaMemcpyDeviceToHost, e->stream),
+                        "D2H"))
+            return PTQ8_ERR_CUDA;
+        e->async_slot ^= 1;
+        return PTQ8_OK;
+    } catch (const std::exception& ex) {
+        return e ? e->fail(strf("forward_async: %s", ex.what()), PTQ8_ERR_CUDA) : PTQ8_ERR_CUDA;
+    }
 }
 
 int ptq8_engine_copy_logits(ptq8_engine* e, int n, float* dst_dev) {

@@ -41,7 +41,7 @@ EXPORTS = (
     "ptq8_engine_create", "ptq8_engine_destroy", "ptq8_engine_last_error", "ptq8_engine_build",
     "ptq8_engine_set_act_mode", "ptq8_engine_set_calib", "ptq8_engine_set_input_shape",
     "ptq8_engine_alloc_scratch", "ptq8_engine_set_stream", "ptq8_engine_set_max_ctas", "ptq8_engine_stream", "ptq8_engine_forward",
-    "ptq8_engine_forward_device", "ptq8_engine_input_buffer", "ptq8_engine_logits_buffer", "ptq8_engine_run", "ptq8_engine_copy_logits",
+    "ptq8_engine_forward_device", "ptq8_engine_forward_async", "ptq8_engine_input_buffer", "ptq8_engine_logits_buffer", "ptq8_engine_run", "ptq8_engine_copy_logits",
     "ptq8_engine_sync", "ptq8_engine_check_device_error", "ptq8_engine_tensor_info", "ptq8_engine_dump",
     "ptq8_engine_n_launches", "ptq8_engine_passes_log", "ptq8_engine_profile",
     "ptq8_load", "ptq8_forward", "ptq8_forward_debug", "ptq8_capture_graph", "ptq8_destroy", "ptq8_last_error",
@@ -102,6 +102,7 @@ def lib() -> ctypes.CDLL:
         "ptq8_engine_stream": (c_void_p, [c_void_p]),
         "ptq8_engine_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
         "ptq8_engine_forward_device": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+        "ptq8_engine_forward_async": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
         "ptq8_engine_input_buffer": (c_void_p, [c_void_p]),
         "ptq8_engine_logits_buffer": (c_void_p, [c_void_p]),
         "ptq8_engine_run": (c_int, [c_void_p, c_int, c_int]),
@@ -302,6 +303,11 @@ class Int8Engine:
     def forward_host_ptr(self, x_ptr: int, n: int, c: int, h: int, w: int, out_ptr: int):
         """Same as forward() on raw host pointers (pinned buffers from the caller)."""
         self._check(lib().ptq8_engine_forward(self._h, ctypes.c_void_p(x_ptr), n, c, h, w, ctypes.c_void_p(out_ptr)))
+
+    def forward_async(self, x_ptr: int, n: int, out_ptr: int):
+        """Pipelined host-buffer forward on raw (pinned) host pointers: enqueue and return;
+        sync() waits.  The next call's input copy overlaps this call's forward."""
+        self._check(lib().ptq8_engine_forward_async(self._h, ctypes.c_void_p(x_ptr), n, ctypes.c_void_p(out_ptr)))
 
     def forward_device(self, x_ptr: int, n: int, logits_ptr: int):
         self._check(lib().ptq8_engine_forward_device(self._h, ctypes.c_void_p(x_ptr), n, ctypes.c_void_p(logits_ptr)))
