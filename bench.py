@@ -173,9 +173,24 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def cpu_baseline(paths, n_img: int, seed: int = 99) -> dict:
+def host_cpu() -> dict:
+    """CPU model name and logical core count of this host."""
+    model = "unknown"
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count() or 1}
+
+
+def cpu_baseline(paths, n_img: int, seed: int = 99, runs: int = 3) -> dict:
     """The reference's CPU integer forward (ref_e2e.py arithmetic: numpy int32 matmul,
-    one core) on a bounded sample of the same workload, timed on this host."""
+    one core) on a bounded sample of the same workload, timed on this host with the
+    reference's CPU protocol (09-ptq-toolkit/tools/stage0_bench.py: warm-up, then the
+    median of `runs` timed runs)."""
     import numpy as np
     from oracle import ptq8_oracle as O
     from ptq_int8_lab_b200 import modelgen as mg
@@ -185,14 +200,18 @@ def cpu_baseline(paths, n_img: int, seed: int = 99) -> dict:
         orc = O.Oracle(m, O.read_ptqc(paths["calib"]), layer_bits=mg.read_layer_plan(paths["plan"]))
         x = np.random.default_rng(seed).standard_normal((n_img, 3, 32, 32)).astype(np.float32)
         orc.forward(x[:1], trace=False)
-        t0 = time.perf_counter()
-        orc.forward(x, trace=False)
-        dt = time.perf_counter() - t0
+        dts = []
+        for _ in range(runs):
+            t0 = time.perf_counter()
+            orc.forward(x, trace=False)
+            dts.append(time.perf_counter() - t0)
     finally:
         O.MATMUL_MODE["mode"] = "blas"
+    dt = sorted(dts)[len(dts) // 2]
     return {"value": n_img / dt, "unit": "images/s", "cores": 1, "kind": "port",
             "sample": f"{n_img} images of the same workload, numpy int32 matmul (06-gpu-int8/cpp/ref_e2e.py:180), "
-                      f"{dt:.1f} s"}
+                      f"median of {runs} runs ({', '.join(f'{t:.2f}' for t in dts)} s) after a warm-up",
+            **host_cpu()}
 
 
 def _ref_worker(args):
@@ -239,7 +258,7 @@ def run_reference(a):
                        "note": "bounded sample per step on host cores"},
             "cpu_baseline": {"value": v, "unit": "images/s", "cores": cores, "kind": "port",
                              "sample": f"{per} images per process x {cores} spawn processes per step, "
-                                       f"numpy int32 matmul as ref_e2e.py:180"},
+                                       f"numpy int32 matmul as ref_e2e.py:180", **host_cpu()},
             "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
