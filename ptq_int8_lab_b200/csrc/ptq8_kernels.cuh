@@ -1108,9 +1108,22 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         } else {
                             if (!code_kept(e, o, h, w)) continue;
                             int8_t* qp = code_ptr(e, o, pq, n, ch, h, w);
+                            if (NOUT <= 1 && !e.dcr_oc) {
+                                // Partial group: channels past tile_end are the code row's padding
+                                // (only the last N tile is partial, and ldq is cout rounded up to
+                                // 32); their constants are zero, so they dequantize to 0 and get
+                                // code 0, the padding's value: all 16 codes go out in one store.
+                                // (Single-output kernels only: in two-output ones the extra path
+                                // costs register spills.)
+                                uint32_t w4[4];
+                                quant16q<true>(y, o == 0 ? qx0 : qx1, s, w4);
+                                *reinterpret_cast<uint4*>(qp) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                            } else {
+                                // positionally decomposed: channels past a position belong to another
 #pragma unroll
-                            for (int j = 0; j < 16; ++j)
-                                if (j < nv) qp[j] = sat8(quant_code(final_val(y[j]), inv, s));
+                                for (int j = 0; j < 16; ++j)
+                                    if (j < nv) qp[j] = sat8(quant_code(final_val(y[j]), inv, s));
+                            }
                         }
                     }
                 }
