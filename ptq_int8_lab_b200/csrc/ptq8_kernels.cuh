@@ -564,13 +564,16 @@ __device__ __forceinline__ void load_res16(const EpiParams& e, size_t pf, int c0
 // 0x4B000000 stays below 2^23, so one OR over the 16 patterns tells whether
 // every accumulator was in range.  Otherwise the rounding conversion is used.
 // `check` false: the caller knows |acc| < 2^22 (128 * sum |w| < 2^22 for every channel).
+// BIASED: v already holds acc + 0x4B400000 (an accumulator that started at the bias;
+// the caller knows |acc| < 2^22, `check` is ignored).
+template <bool BIASED = false>
 __device__ __forceinline__ void dequant16(const uint32_t (&v)[16], const float2* fb, int act, float (&y)[16],
                                           bool check = true) {
     uint32_t range = 0;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        const uint32_t bits = v[j] + static_cast<uint32_t>(kRoundMagicBits);
-        if (check) range |= bits ^ 0x4B000000u;
+        const uint32_t bits = BIASED ? v[j] : v[j] + static_cast<uint32_t>(kRoundMagicBits);
+        if (check && !BIASED) range |= bits ^ 0x4B000000u;
         y[j] = __uint_as_float(bits);
     }
     if (range < 0x800000u) {
@@ -1305,8 +1308,9 @@ __global__ void dw_conv_kernel(const int8_t* __restrict__ in, int ldi, const int
 // word per channel holding the column's 3 taps, which every position of the
 // strip that uses the column multiplies by the matching weight column with one
 // dp4a.  Integer sums are exact, so the order of taps does not change the
-// accumulator; |acc| <= 9 * 128 * 128 < 2^22 (float conversion without range
-// check).
+// accumulator; |acc| <= 9 * 128 * 128 < 2^22, so the accumulators start at the
+// float-conversion bias 0x4B400000 and their final bits are already those of
+// 1.5*2^23 + acc (no range check, no add in the epilogue).
 //
 // Epilogue: y = fadd(fmul(float(acc), factor), bias), then the activation and
 // the quantizer's clamp as one clamp: relu6 then clip to [y_lo, y_hi] is
@@ -1457,7 +1461,7 @@ __global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const in
         const int nstrip = k * d.R * d.strips;
         const uint8_t* sb = dw_smem + stage * d.stage_bytes + c0;
         for (int sl = static_cast<int>(threadIdx.x) / G4; sl < nstrip; sl += per_pass) {
-            const int kk = static_cast<int>(fdiv(static_cast<uint32_t>(sl), d.fd_rs));
+            const int kk = k == 1 ? 0 : static_cast<int>(fdiv(static_cast<uint32_t>(sl), d.fd_rs));
             const int rem = sl - kk * d.R * d.strips;
             const int rr = static_cast<int>(fdiv(static_cast<uint32_t>(rem), d.fd_strips));
             const int cs = rem - rr * d.strips;
@@ -1466,7 +1470,7 @@ __global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const in
 #pragma unroll
             for (int t = 0; t < T; ++t)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) acc[t][c] = 0;
+                for (int c = 0; c < 4; ++c) acc[t][c] = kRoundMagicBits;   // float-conversion bias (see dequant16)
 #pragma unroll
             for (int j = 0; j < S * (T - 1) + 3; ++j) {
                 const uint8_t* col = base + j * ldi;
@@ -1491,11 +1495,11 @@ __global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const in
             for (int t = 0; t < 4; ++t)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    v[4 * t + c] = t < T ? static_cast<uint32_t>(acc[t < T ? t : 0][c]) : 0u;
+                    v[4 * t + c] = t < T ? static_cast<uint32_t>(acc[t < T ? t : 0][c]) : kRoundMagicBits;
                     fb[4 * t + c] = fbc[c];
                 }
             float y[16];
-            dequant16(v, fb, 0, y, false);
+            dequant16<true>(v, fb, 0, y, false);
             if (ACT != 0) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.0f);
