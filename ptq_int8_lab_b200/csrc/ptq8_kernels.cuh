@@ -1159,8 +1159,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 // map (border rows are never written and stay zero) with k = (i*KW + j)*C + c,
 // codes of the stem's scale, zero for out-of-image taps and k >= KH*KW*C.
 // One CTA per band of `rows` output rows of one image.  The input band is read
-// once (one warp per band row, coalesced) and quantized once into shared
-// memory with its zero padding; a table maps k to its offset in the band; then
+// once (consecutive threads take consecutive band elements, 16 loads in flight
+// per thread) and quantized once into shared memory with its zero padding; a
+// table maps k to its offset in the band; then
 // each thread assembles the kpad-byte im2col row of one output pixel and writes
 // it with 16-byte stores (consecutive pixels: consecutive rows).
 __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restrict__ out, int N, int C, int H,
@@ -1186,19 +1187,28 @@ __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restri
         }
         koff[k] = o;
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    // The band, element e = (c * band_h + bh) * band_w + bw, in rounds of 16 elements
+    // per thread: all 16 loads are issued before the first is quantized, so a round
+    // waits for one memory latency (a warp per band row, row after row, waited for one
+    // per row).  Out-of-image elements are the zero padding.
     const int ih0 = r0 * SH - PH, iw0 = -PW;
-    for (int rr = warp; rr < C * band_h; rr += nwarps) {
-        const int c = rr / band_h, bh = rr - (rr / band_h) * band_h;
-        const int ih = ih0 + bh;
-        const bool row_in = ih >= 0 && ih < H;
-        const float* xr = x + ((static_cast<size_t>(n) * C + c) * H + (row_in ? ih : 0)) * W;
-        int8_t* br = band + rr * band_w;
-        for (int bw = lane; bw < band_w; bw += 32) {
-            const int iw = iw0 + bw;
-            int q = 0;
-            if (row_in && iw >= 0 && iw < W) q = sat8(quant_code(__ldg(xr + iw), inv, s));
-            br[bw] = static_cast<int8_t>(q);
+    const float* xn = x + static_cast<size_t>(n) * C * H * W;
+    constexpr int kRound = 16;
+    for (int e0 = 0; e0 < band_bytes; e0 += kRound * static_cast<int>(blockDim.x)) {
+        float v[kRound];
+#pragma unroll
+        for (int m = 0; m < kRound; ++m) {
+            const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+            const int rr = e / band_w, bw = e - rr * band_w;
+            const int c = rr / band_h, bh = rr - c * band_h;
+            const int ih = ih0 + bh, iw = iw0 + bw;
+            const bool in = e < band_bytes && ih >= 0 && ih < H && iw >= 0 && iw < W;
+            v[m] = in ? __ldg(xn + (static_cast<size_t>(c) * H + ih) * W + iw) : 0.0f;
+        }
+#pragma unroll
+        for (int m = 0; m < kRound; ++m) {
+            const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+            if (e < band_bytes) band[e] = static_cast<int8_t>(sat8(quant_code(v[m], inv, s)));
         }
     }
     __syncthreads();
