@@ -1214,24 +1214,29 @@ __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restri
     __syncthreads();
     const int npix = (r1 - r0) * OW;
     int8_t* obase = out + ((static_cast<size_t>(n) * (OH + 2) + r0 + 1) * (OW + 2) + 1) * kpad;
-    for (int p = threadIdx.x; p < npix; p += blockDim.x) {
-        const int ohl = p / OW, ow = p - (p / OW) * OW;
-        const int8_t* bp = band + ohl * SH * band_w + ow * SW;
-        uint4* op = reinterpret_cast<uint4*>(obase + static_cast<size_t>(ohl * (OW + 2) + ow) * kpad);
-        for (int k0 = 0; k0 < kpad; k0 += 16) {
+    // 16 bytes of every pixel's row at a time: their 16 band offsets stay in registers
+    // for all of this thread's pixels
+    for (int k0 = 0; k0 < kpad; k0 += 16) {
+        int ko[16];
+#pragma unroll
+        for (int b = 0; b < 16; ++b) ko[b] = koff[k0 + b];
+        for (int p = threadIdx.x; p < npix; p += blockDim.x) {
+            const int ohl = p / OW, ow = p - (p / OW) * OW;
+            const int8_t* bp = band + ohl * SH * band_w + ow * SW;
             uint32_t wv[4];
 #pragma unroll
             for (int wd = 0; wd < 4; ++wd) {
                 uint32_t packed = 0;
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
-                    const int o = koff[k0 + wd * 4 + b];
+                    const int o = ko[wd * 4 + b];
                     const uint32_t q = o >= 0 ? static_cast<uint8_t>(bp[o]) : 0u;
                     packed |= q << (8 * b);
                 }
                 wv[wd] = packed;
             }
-            op[k0 >> 4] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            reinterpret_cast<uint4*>(obase + static_cast<size_t>(ohl * (OW + 2) + ow) * kpad)[k0 >> 4] =
+                make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
     }
 }
