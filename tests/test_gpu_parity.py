@@ -77,3 +77,13 @@ def test_ragged_depthwise_channels(make_model):
     paths = make_model("mobilenet_v2", seed=4, bn="data", settings=RAGGED_MV2)
     eng, tr, om, logits = _run(paths, 9, seed=13)
     compare(eng, tr, om, 9, logits)
+
+
+@pytest.mark.parametrize("key,kw", [("resnet18", dict(seed=0, bn="data")),
+                                    ("mobilenet_v2", dict(seed=1, bn="data"))])
+def test_batch_one(make_model, key, kw):
+    """A single image: one partial M tile per conv, depthwise units holding fewer images
+    than planned, a one-CTA head."""
+    paths = make_model(key, **kw)
+    eng, tr, om, logits = _run(paths, 1, seed=17)
+    compare(eng, tr, om, 1, logits)
