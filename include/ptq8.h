@@ -138,7 +138,9 @@ int ptq8_engine_forward(ptq8_engine* e, const float* x_host, int n, int c, int h
  * copy has landed, and the D2H copy of the logits; returns without waiting.  The H2D of
  * call k+1 overlaps the forward of call k.  ptq8_engine_sync() waits for every enqueued
  * call.  x_host (pinned, for the copies to overlap) must stay unchanged and logits_host
- * unread until then.  Same logits as ptq8_engine_forward. */
+ * unread until then.  Same logits as ptq8_engine_forward.  The engine's other calls
+ * that take or run on an input (forward, forward_device, run, input_buffer, profile,
+ * ptq8_forward / ptq8_forward_debug) first wait for pipelined copies still in flight. */
 int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float* logits_host);
 /* Device-pointer forward (fp32 NCHW input, fp32 [n][fc_out] logits); enqueued
  * on the engine stream, not synchronized. */

@@ -1727,11 +1727,17 @@ int ptq8_engine_set_stream(ptq8_engine* e, void* stream) {
 
 void* ptq8_engine_stream(ptq8_engine* e) { return e ? static_cast<void*>(e->stream) : nullptr; }
 
-float* ptq8_engine_input_buffer(ptq8_engine* e) { return e ? e->d_input : nullptr; }
+float* ptq8_engine_input_buffer(ptq8_engine* e) {
+    if (!e) return nullptr;
+    // a pipelined call's copy into this buffer may still be in flight
+    if (e->copy_stream) cudaStreamSynchronize(e->copy_stream);
+    return e->d_input;
+}
 float* ptq8_engine_logits_buffer(ptq8_engine* e) { return e ? e->d_logits : nullptr; }
 
 int ptq8_engine_run(ptq8_engine* e, int n, int use_graph) {
     if (!e) return PTQ8_ERR_INVALID;
+    if (e->copy_stream && !e->cuda_ok(cudaStreamSynchronize(e->copy_stream), "copy stream")) return PTQ8_ERR_CUDA;
     return launch(e, n, use_graph != 0);
 }
 
@@ -1939,6 +1945,7 @@ int ptq8_engine_profile(ptq8_engine* e, int n, int iters, float* ms, double* mac
         if (rc) return rc;
     }
     if (n <= 0 || n > e->max_batch) return e->fail("profile: batch outside the allocated range");
+    if (e->copy_stream && !e->cuda_ok(cudaStreamSynchronize(e->copy_stream), "copy stream")) return PTQ8_ERR_CUDA;
     const int ns = (int)e->steps.size() + 1;
     if (n_steps) *n_steps = ns;
     if (cap < ns) return e->fail(strf("profile: needs %d entries", ns));
