@@ -316,7 +316,9 @@ def make_modelgen_pin():
 
 
 if __name__ == "__main__":
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/ptq-int8-lab")
+    ref = Path(sys.argv[1])
     setup(ref)
     make_kats()
     make_r18_tiny()
