@@ -74,7 +74,10 @@ int ptq8_quantize_weight(const float* w, int cout, int k, int bits, int8_t* code
 
 /* Activation codes computed on `device` by the engine's own device quantizer
  * (the epilogue path): codes[i] = clip(round_half_away(double(x[i]) / s), -128, 127)
- * with s = ptq8_act_scale(lo, hi, 8, mode) (ref_int8.py:89-91).  Test entry point. */
+ * with s = ptq8_act_scale(lo, hi, 8, mode) (ref_int8.py:89-91).  Test entry point.
+ * The range is checked like load_ptqc checks PTQC entries (ptq_model.h:425-503):
+ * non-finite lo/hi, lo > hi, or a mode other than PTQ8_ACT_ABSMAX / PTQ8_ACT_MINMAX
+ * return PTQ8_ERR_INVALID before any device work. */
 int ptq8_quantize_device(int device, const float* x_host, size_t n, float lo, float hi, int mode, int8_t* codes);
 
 /* Same codes as ptq8_quantize_device, but the call allocates no device memory
@@ -87,13 +90,14 @@ int ptq8_quantize_device(int device, const float* x_host, size_t n, float lo, fl
  * The input and output stay the caller's host buffers.  The device staging for
  * them is a fixed array inside the library, one per device, holding at most
  * PTQ8_NOALLOC_MAX_VALUES values (4 MiB of floats + 1 MiB of codes); a larger n
- * is rejected with PTQ8_ERR_INVALID and a message in err.  The first call on a
- * device looks that array up (with the device current) and so does set-up work:
- * make it before any stream capture.  All calls on a device share the array and
- * leave their data in it, so calls that overlap in time (two host threads on the
- * same device) race and must be serialised by the caller.  Copies and the kernel
- * run on the legacy default stream; the call returns when the codes are on the
- * host.  err (may be NULL) receives "" on success. */
+ * is rejected with PTQ8_ERR_INVALID and a message in err, and so is a range or mode
+ * that ptq8_quantize_device rejects.  Every call looks the array's device address up
+ * (cudaGetSymbolAddress, with the device current), so the first call on a device
+ * loads the module there: make it before any stream capture.  All calls on a device
+ * share the array and leave their data in it, so calls that overlap in time (two host
+ * threads on the same device) race and must be serialised by the caller.  Copies and
+ * the kernel run on the legacy default stream; the call returns when the codes are on
+ * the host.  err (may be NULL) receives "" on success. */
 #define PTQ8_NOALLOC_MAX_VALUES (1u << 20)
 int ptq8_quantize_device_noalloc(int device, const float* x_host, size_t n, float lo, float hi, int mode,
                                  int8_t* codes, char* err, size_t errlen);
@@ -153,8 +157,19 @@ int ptq8_engine_run(ptq8_engine* e, int n, int use_graph);
 /* Async device-to-device copy of the last forward's logits ([n][fc_out]) on the engine stream. */
 int ptq8_engine_copy_logits(ptq8_engine* e, int n, float* dst_dev);
 int ptq8_engine_sync(ptq8_engine* e);
-/* Reads and clears the device error word set by bounded waits. */
+/* Reads and clears this engine's device error word, set by bounded waits that ran out
+ * (PTQ8_ERR_TIMEOUT; each engine has its own word, so one engine's timeout never
+ * aborts or reports through another).  No counterpart in the reference (its kernels
+ * have no waits; CUDA errors exit, int8_engine.cuh:109-117). */
 int ptq8_engine_check_device_error(ptq8_engine* e);
+/* Failure-detection test hook, no counterpart in the reference.  Sets the limit of
+ * every bounded device wait of this engine's kernels in clock cycles (0: the default,
+ * about 2 s) and, when stall_first_load is nonzero, makes the first operand load of
+ * the forward's first tensor-core conv (CTA 0) never arrive, so that the waits on it
+ * run out: the forward then reports PTQ8_ERR_TIMEOUT through
+ * ptq8_engine_check_device_error / ptq8_engine_sync / ptq8_engine_forward instead of
+ * hanging, and the context stays usable.  Drops captured graphs. */
+int ptq8_engine_set_wait_test(ptq8_engine* e, long long wait_limit_cycles, int stall_first_load);
 
 /* Parity dumps (replaces forward(..., stop_after_block, mid_out),
  * int8_engine.cuh:429 and locate_block.cpp): what 0 = int8 input codes of conv
@@ -162,6 +177,10 @@ int ptq8_engine_check_device_error(ptq8_engine* e);
  * the fp32 map fed to the pooling head (NHWC).  shape4 = {N_max, H, W, ld}. */
 int ptq8_engine_tensor_info(ptq8_engine* e, int what, int index, int* shape4);
 int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst, size_t bytes);
+/* The same for images [n0, n0 + n) of the last forward (the reference oracle runs and
+ * dumps a batch chunk by chunk, 06-gpu-int8/cpp/ref_e2e.py:308-329): parity checks of a
+ * full-size batch without copying whole multi-GB maps to the host. */
+int ptq8_engine_dump_range(ptq8_engine* e, int what, int index, int n0, int n, void* host_dst, size_t bytes);
 /* Per-launch timing (CUDA events on the engine stream, `iters` back-to-back
  * launches of each step, not graph-captured) with each step's algorithmic work:
  * ms[i], macs[i], bytes[i], kind[i] (0 stem im2col + GEMM, 1 tensor-core conv,

@@ -177,6 +177,11 @@ struct ptq8_engine {
     float* d_logits = nullptr;
     float* d_fc_w = nullptr;
     float* d_fc_b = nullptr;
+    // device error word of this engine's kernels (bounded waits that ran out), the wait
+    // limit they get, and the failure-detection test switch (ptq8_engine_set_wait_test)
+    int* d_err = nullptr;
+    long long wait_limit = kWaitLimitCycles;
+    int stall_first_load = 0;
     std::vector<void*> allocs;
     std::map<int, cudaGraphExec_t> graphs;
     std::vector<std::string> passes_log;
@@ -753,10 +758,14 @@ int finalize(ptq8_engine* e, int max_batch) {
     for (void* p : e->allocs) cudaFree(p);
     e->allocs.clear();
     e->d_input2 = nullptr;
+    e->d_err = nullptr;
     e->async_slot = 0;
     e->planned = false;
     int rc = plan(e);
     if (rc) return rc;
+    if (!e->dalloc(&e->d_err, sizeof(int), "alloc device error word") ||
+        !e->cuda_ok(cudaMemset(e->d_err, 0, sizeof(int)), "clear device error word"))
+        return PTQ8_ERR_CUDA;
     const size_t NB = (size_t)max_batch;
     // the kernels decode positions in 32-bit arithmetic
     for (const Value& v : e->vals)
@@ -1131,6 +1140,8 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         d.fd_strips = make_fastdiv(d.strips);
         d.fd_rs = make_fastdiv(st.dw_R * d.strips);
         d.fd_bands = make_fastdiv(d.bands);
+        d.err = e->d_err;
+        d.wait_limit = e->wait_limit;
         const int grid = std::max(1, std::min(d.n_units, st.dw_ctas));
         launch_pdl((DwKernel)st.dw_kfn, dim3(grid), dim3(st.dw_cons + 32), (size_t)d.n_stages * d.stage_bytes, s,
                    vin.codes[vin.code_index(st.s_in)], (const uint4*)st.d_dwt, d, ep);
@@ -1208,6 +1219,15 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.stages = st.stages;
     g.b_resident = st.b_resident;
     g.b_bytes = (uint32_t)(st.bn * st.cb);
+    g.err = e->d_err;
+    g.wait_limit = e->wait_limit;
+    g.stall_first_load = 0;
+    if (e->stall_first_load) {   // the forward's first tensor-core conv only
+        size_t first = e->steps.size();
+        for (size_t k = 0; k < e->steps.size() && first == e->steps.size(); ++k)
+            if ((e->steps[k].kind == K_TC || e->steps[k].kind == K_STEM_IM2COL) && !e->steps[k].fused) first = k;
+        g.stall_first_load = si == first ? 1 : 0;
+    }
     const int gx = e->max_ctas > 0 ? std::min(st.grid_x, std::max(1, e->max_ctas / st.n_ntiles)) : st.grid_x;
     dim3 grid((unsigned)std::min(g.m_tiles, gx), (unsigned)st.n_ntiles);
     CUtensorMap ma = st.map_a, mb = st.map_b, mxa = st.map_xa, mxb = st.map_xb;
@@ -1331,6 +1351,37 @@ int launch(ptq8_engine* e, int n, bool use_graph) {
     return PTQ8_OK;
 }
 
+// Work just enqueued on the engine stream reads input slot 0 (d_input): a pipelined
+// forward must not overwrite that slot before it has run, so the slot's "free" event
+// moves past it (once the pipelined path exists; until then nothing copies into the
+// slot from another stream).
+void mark_input_read(ptq8_engine* e) {
+    if (e->ev_free[0]) cudaEventRecord(e->ev_free[0], e->stream);
+}
+
+// A PTQC-style range the device quantizer accepts: the rules ptq8_engine_set_calib
+// and load_ptqc enforce (finite, lo <= hi; ptq_model.h:425-503), a known scale mode,
+// and a finite positive scale (the precondition of make_qparams).
+bool quant_range_ok(float lo, float hi, int mode, std::string& why) {
+    if (mode != ACT_ABSMAX && mode != ACT_MINMAX) {
+        why = strf("act mode %d: must be %d (absmax) or %d (minmax)", mode, (int)ACT_ABSMAX, (int)ACT_MINMAX);
+        return false;
+    }
+    if (!std::isfinite(lo) || !std::isfinite(hi)) {
+        why = "calibration range not finite";
+        return false;
+    }
+    if (lo > hi) {
+        why = "calibration range lo > hi";
+        return false;
+    }
+    if (!qparams_scale_ok(act_scale_from_range(lo, hi, 8, mode))) {
+        why = "activation scale not finite and positive";
+        return false;
+    }
+    return true;
+}
+
 void copy_err(const std::string& m, char* err, size_t errlen) {
     if (err && errlen) {
         std::snprintf(err, errlen, "%s", m.c_str());
@@ -1350,24 +1401,17 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocCodesOf
 
 namespace {
 
-constexpr int kNoAllocMaxDevices = 64;
-std::mutex g_noalloc_mu;
-unsigned char* g_noalloc_ptr[kNoAllocMaxDevices] = {};
-
-// Address of g_noalloc_scratch on `device` (which must be current), looked up on
-// the first call for that device and remembered.
-unsigned char* noalloc_scratch(int device, std::string& why) {
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_ptr[device]) {
-        void* p = nullptr;
-        const cudaError_t ce = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (ce != cudaSuccess || !p) {
-            why = strf("cudaGetSymbolAddress of the fixed scratch failed: %s", cudaGetErrorString(ce));
-            return nullptr;
-        }
-        g_noalloc_ptr[device] = static_cast<unsigned char*>(p);
+// Device address of g_noalloc_scratch on the current device.  Looked up on every
+// call (the lookup allocates nothing): a remembered address would go stale when the
+// device's primary context is reset and the module reloaded.
+unsigned char* noalloc_scratch(std::string& why) {
+    void* p = nullptr;
+    const cudaError_t ce = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (ce != cudaSuccess || !p) {
+        why = strf("cudaGetSymbolAddress of the fixed scratch failed: %s", cudaGetErrorString(ce));
+        return nullptr;
     }
-    return g_noalloc_ptr[device];
+    return static_cast<unsigned char*>(p);
 }
 
 }  // namespace
@@ -1499,6 +1543,8 @@ int ptq8_quantize_weight(const float* w, int cout, int k, int bits, int8_t* code
 
 int ptq8_quantize_device(int device, const float* x_host, size_t n, float lo, float hi, int mode, int8_t* codes) {
     if (!x_host || !codes) return PTQ8_ERR_INVALID;
+    std::string why;
+    if (!quant_range_ok(lo, hi, mode, why)) return PTQ8_ERR_INVALID;
     if (cudaSetDevice(device) != cudaSuccess) return PTQ8_ERR_CUDA;
     const double s = act_scale_from_range(lo, hi, 8, mode);
     float* dx = nullptr;
@@ -1528,8 +1574,13 @@ int ptq8_quantize_device_noalloc(int device, const float* x_host, size_t n, floa
         copy_err("null input or output pointer", err, errlen);
         return PTQ8_ERR_INVALID;
     }
-    if (device < 0 || device >= kNoAllocMaxDevices) {
-        copy_err(strf("device %d out of range [0, %d)", device, kNoAllocMaxDevices), err, errlen);
+    if (device < 0) {
+        copy_err(strf("device %d is negative", device), err, errlen);
+        return PTQ8_ERR_INVALID;
+    }
+    std::string bad;
+    if (!quant_range_ok(lo, hi, mode, bad)) {
+        copy_err(bad, err, errlen);
         return PTQ8_ERR_INVALID;
     }
     if (n > static_cast<size_t>(PTQ8_NOALLOC_MAX_VALUES)) {
@@ -1544,7 +1595,7 @@ int ptq8_quantize_device_noalloc(int device, const float* x_host, size_t n, floa
         return PTQ8_ERR_CUDA;
     }
     std::string why;
-    unsigned char* base = noalloc_scratch(device, why);
+    unsigned char* base = noalloc_scratch(why);
     if (!base) {
         copy_err(why, err, errlen);
         return PTQ8_ERR_CUDA;
@@ -1713,6 +1764,10 @@ int ptq8_engine_set_max_ctas(ptq8_engine* e, int max_ctas) {
 
 int ptq8_engine_set_stream(ptq8_engine* e, void* stream) {
     if (!e) return PTQ8_ERR_INVALID;
+    // work still queued on the old stream (or input copies on the copy stream) uses the
+    // activations, logits and input slots the new stream is about to reuse
+    if (e->stream && !e->cuda_ok(cudaStreamSynchronize(e->stream), "sync old stream")) return PTQ8_ERR_CUDA;
+    if (e->copy_stream && !e->cuda_ok(cudaStreamSynchronize(e->copy_stream), "sync copy stream")) return PTQ8_ERR_CUDA;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
     if (e->own_stream && e->stream) cudaStreamDestroy(e->stream);
@@ -1729,8 +1784,10 @@ void* ptq8_engine_stream(ptq8_engine* e) { return e ? static_cast<void*>(e->stre
 
 float* ptq8_engine_input_buffer(ptq8_engine* e) {
     if (!e) return nullptr;
-    // a pipelined call's copy into this buffer may still be in flight
+    // a pipelined call's copy into this buffer may still be in flight, and a forward
+    // queued on the engine stream may still be reading it
     if (e->copy_stream) cudaStreamSynchronize(e->copy_stream);
+    if (e->stream) cudaStreamSynchronize(e->stream);
     return e->d_input;
 }
 float* ptq8_engine_logits_buffer(ptq8_engine* e) { return e ? e->d_logits : nullptr; }
@@ -1738,7 +1795,9 @@ float* ptq8_engine_logits_buffer(ptq8_engine* e) { return e ? e->d_logits : null
 int ptq8_engine_run(ptq8_engine* e, int n, int use_graph) {
     if (!e) return PTQ8_ERR_INVALID;
     if (e->copy_stream && !e->cuda_ok(cudaStreamSynchronize(e->copy_stream), "copy stream")) return PTQ8_ERR_CUDA;
-    return launch(e, n, use_graph != 0);
+    const int rc = launch(e, n, use_graph != 0);
+    if (!rc) mark_input_read(e);
+    return rc;
 }
 
 int ptq8_engine_forward_device(ptq8_engine* e, const float* x_dev, int n, float* logits_dev) {
@@ -1755,6 +1814,7 @@ int ptq8_engine_forward_device(ptq8_engine* e, const float* x_dev, int n, float*
         return PTQ8_ERR_CUDA;
     int rc = launch(e, n, true);
     if (rc) return rc;
+    mark_input_read(e);
     if (logits_dev != e->d_logits &&
         !e->cuda_ok(cudaMemcpyAsync(logits_dev, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
                                     cudaMemcpyDeviceToDevice, e->stream),
@@ -1779,6 +1839,7 @@ int ptq8_engine_forward(ptq8_engine* e, const float* x_host, int n, int c, int h
         return PTQ8_ERR_CUDA;
     int rc = launch(e, n, true);
     if (rc) return rc;
+    mark_input_read(e);
     if (!e->cuda_ok(cudaMemcpyAsync(logits_host, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
                                     cudaMemcpyDeviceToHost, e->stream),
                     "D2H"))
@@ -1802,7 +1863,10 @@ int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float*
                 return PTQ8_ERR_CUDA;
             for (int k = 0; k < 2; ++k)
                 if (!e->cuda_ok(cudaEventCreateWithFlags(&e->ev_staged[k], cudaEventDisableTiming), "event") ||
-                    !e->cuda_ok(cudaEventCreateWithFlags(&e->ev_free[k], cudaEventDisableTiming), "event"))
+                    !e->cuda_ok(cudaEventCreateWithFlags(&e->ev_free[k], cudaEventDisableTiming), "event") ||
+                    // work already queued on the engine stream (a forward_device or run graph
+                    // reading slot 0) must finish before the first pipelined copy overwrites a slot
+                    !e->cuda_ok(cudaEventRecord(e->ev_free[k], e->stream), "record free"))
                     return PTQ8_ERR_CUDA;
         }
         if (!e->d_input2 &&
@@ -1850,13 +1914,28 @@ int ptq8_engine_sync(ptq8_engine* e) {
 
 int ptq8_engine_check_device_error(ptq8_engine* e) {
     if (!e) return PTQ8_ERR_INVALID;
+    if (!e->d_err) return PTQ8_OK;   // nothing has run yet
     int v = 0;
-    if (!e->cuda_ok(cudaMemcpyFromSymbol(&v, g_ptq8_error, sizeof(int)), "read device error")) return PTQ8_ERR_CUDA;
+    // ordered after this engine's enqueued work (its stream is non-blocking)
+    if (!e->cuda_ok(cudaMemcpyAsync(&v, e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->stream), "read device error") ||
+        !e->cuda_ok(cudaStreamSynchronize(e->stream), "read device error"))
+        return PTQ8_ERR_CUDA;
     if (v != 0) {
-        const int z = 0;
-        cudaMemcpyToSymbol(g_ptq8_error, &z, sizeof(int));
+        if (!e->cuda_ok(cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream), "clear device error") ||
+            !e->cuda_ok(cudaStreamSynchronize(e->stream), "clear device error"))
+            return PTQ8_ERR_CUDA;
         return e->fail(strf("device wait timed out (code %d); results of this forward are invalid", v), PTQ8_ERR_TIMEOUT);
     }
+    return PTQ8_OK;
+}
+
+int ptq8_engine_set_wait_test(ptq8_engine* e, long long wait_limit_cycles, int stall_first_load) {
+    if (!e || wait_limit_cycles < 0) return PTQ8_ERR_INVALID;
+    if (e->stream && !e->cuda_ok(cudaStreamSynchronize(e->stream), "sync")) return PTQ8_ERR_CUDA;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);   // captured with the old parameters
+    e->graphs.clear();
+    e->wait_limit = wait_limit_cycles > 0 ? wait_limit_cycles : kWaitLimitCycles;
+    e->stall_first_load = stall_first_load ? 1 : 0;
     return PTQ8_OK;
 }
 
@@ -1887,8 +1966,13 @@ int ptq8_engine_tensor_info(ptq8_engine* e, int what, int index, int* shape4) {
 }
 
 int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst, size_t bytes) {
+    return ptq8_engine_dump_range(e, what, index, 0, n, host_dst, bytes);
+}
+
+int ptq8_engine_dump_range(ptq8_engine* e, int what, int index, int n0, int n, void* host_dst, size_t bytes) {
     try {
-        if (!e || !e->planned || !host_dst || n <= 0 || n > e->max_batch) return PTQ8_ERR_INVALID;
+        if (!e || !e->planned || !host_dst || n0 < 0 || n <= 0 || n > e->max_batch || n0 > e->max_batch - n)
+            return PTQ8_ERR_INVALID;
         int shp[4];
         int rc = ptq8_engine_tensor_info(e, what, index, shp);
         if (rc) return rc;
@@ -1901,7 +1985,7 @@ int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst,
             if (st.kind == K_STEM_IM2COL) {   // drop the border rows of the bordered im2col map
                 const size_t row = (size_t)st.ow * st.kpad, prow = (size_t)(st.ow + 2) * st.kpad;
                 for (int i = 0; i < n; ++i) {
-                    const int8_t* s0 = st.d_im2col + ((size_t)i * (st.oh + 2) + 1) * prow + st.kpad;
+                    const int8_t* s0 = st.d_im2col + ((size_t)(n0 + i) * (st.oh + 2) + 1) * prow + st.kpad;
                     int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * st.oh * row;
                     if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, st.oh, cudaMemcpyDeviceToHost), "dump"))
                         return PTQ8_ERR_CUDA;
@@ -1915,22 +1999,26 @@ int ptq8_engine_dump(ptq8_engine* e, int what, int index, int n, void* host_dst,
             // drop the one-pixel border: per image, H rows of W*ld bytes out of (H+2) x (W+2)*ld
             const size_t row = (size_t)W * v.ldq, prow = (size_t)(W + 2) * v.ldq;
             for (int i = 0; i < n; ++i) {
-                const int8_t* s0 = src + ((size_t)i * (H + 2) + 1) * prow + v.ldq;
+                const int8_t* s0 = src + ((size_t)(n0 + i) * (H + 2) + 1) * prow + v.ldq;
                 int8_t* d0 = static_cast<int8_t*>(host_dst) + (size_t)i * H * row;
                 if (!e->cuda_ok(cudaMemcpy2D(d0, row, s0, prow, row, H, cudaMemcpyDeviceToHost), "dump"))
                     return PTQ8_ERR_CUDA;
             }
             return PTQ8_OK;
         }
-        // the device map is in the f32_off layout: copy whole blocks, then reorder to NHWC
+        // the device map is in the f32_off layout (whole 32-position blocks of all channels,
+        // or plain NHWC): copy the blocks covering positions [p0, p1), then reorder to NHWC
         const Value& fv = e->vals[e->final_val];
-        const size_t npos = (size_t)n * shp[1] * shp[2];
-        std::vector<float> raw(((npos + 31) & ~(size_t)31) * fv.c);
-        if (!e->cuda_ok(cudaMemcpy(raw.data(), fv.f32, raw.size() * sizeof(float), cudaMemcpyDeviceToHost), "dump"))
+        const size_t hw = (size_t)shp[1] * shp[2];
+        const size_t p0 = (size_t)n0 * hw, p1 = p0 + (size_t)n * hw;
+        const size_t b0 = p0 & ~(size_t)31, b1 = (p1 + 31) & ~(size_t)31;
+        std::vector<float> raw((b1 - b0) * fv.c);
+        if (!e->cuda_ok(cudaMemcpy(raw.data(), fv.f32 + b0 * fv.c, raw.size() * sizeof(float), cudaMemcpyDeviceToHost),
+                        "dump"))
             return PTQ8_ERR_CUDA;
         float* dst = static_cast<float*>(host_dst);
-        for (size_t p = 0; p < npos; ++p)
-            for (int c = 0; c < fv.c; ++c) dst[p * fv.c + c] = raw[f32_off(p, c, fv.c)];
+        for (size_t p = p0; p < p1; ++p)
+            for (int c = 0; c < fv.c; ++c) dst[(p - p0) * fv.c + c] = raw[f32_off(p - b0, c, fv.c)];
         return PTQ8_OK;
     } catch (const std::exception& ex) {
         return e->fail(std::string("dump: ") + ex.what());

@@ -27,9 +27,9 @@
 
 namespace ptq8 {
 
-// Sticky device error word: a bounded wait that ran out records where.
-__device__ int g_ptq8_error;
-
+// Codes a bounded wait that ran out records in its engine's device error word
+// (an int in engine-owned device memory, passed to every kernel that waits, so
+// one engine's timeout never aborts another engine's kernels).
 enum : int {
     ERR_NONE = 0,
     ERR_WAIT_EMPTY = 1,
@@ -38,8 +38,8 @@ enum : int {
     ERR_DRAIN = 4,
 };
 
-// About 2 s at the B200 boost clock; no wait in these kernels is expected to
-// take more than microseconds.
+// Default wait limit: about 2 s at the B200 boost clock; no wait in these
+// kernels is expected to take more than microseconds.
 constexpr long long kWaitLimitCycles = 4000000000LL;
 
 // ------------------------------------------------------------------ PTX helpers
@@ -87,19 +87,20 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait for the phase with the given parity to complete: false after
+// `limit` clock cycles without completion.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long limit) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try(bar, parity)) return true;
-        if (clock64() - t0 > kWaitLimitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     }
 }
 
 // The same wait by every lane of a converged warp; the result is made warp-uniform.
-__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity) {
-    const bool ok = mbar_wait(bar, parity);
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, long long limit) {
+    const bool ok = mbar_wait(bar, parity, limit);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -368,7 +369,12 @@ struct QParams {
     float inv_lo, inv_hi, y_lo, y_hi;
 };
 
+// Precondition: s finite and positive (callers validate the range first; an infinite
+// or NaN scale would leave the bracketing loops below without an exit).
+inline bool qparams_scale_ok(double s) { return std::isfinite(s) && s > 0.0; }
+
 inline QParams make_qparams(double s) {
+    if (!qparams_scale_ok(s)) return {0.0f, 0.0f, 0.0f, 0.0f};
     const double inv = 1.0 / s;
     float lo = static_cast<float>(inv * (1.0 - 0x1p-22));
     float hi = static_cast<float>(inv * (1.0 + 0x1p-22));
@@ -703,6 +709,13 @@ struct ConvGeom {
     FastDiv fd_wp;              // mode 1: Wp
     FastDiv fd_tiles_w;         // mode 0: tiles along W
     FastDiv fd_tiles_h;         // mode 0: tiles along H
+    // failure detection: the engine's device error word (a CTA that finds it set at start
+    // skips its work), the bounded-wait limit in clock cycles, and a test switch that makes
+    // the first A load of CTA (0, 0) never arrive (its expect_tx is posted, the copy is not
+    // issued), so the waits on that stage run out and report instead of hanging
+    int* err;
+    long long wait_limit;
+    int stall_first_load;
 };
 
 constexpr int kEpiWarps = 16;                      // 4 per TMEM lane quadrant
@@ -733,7 +746,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     __shared__ __align__(8) uint64_t bars[2 * kMaxStages + 18];  // a_full, a_empty, b_full, acc_full[8], acc_empty[8], done
     __shared__ uint32_t tslot;
     // A wait of an earlier CTA already ran out: skip the work (block-uniform decision).
-    if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile int*>(&g_ptq8_error);
+    if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile int*>(g.err);
     __syncthreads();
     if (s_abort) return;
 
@@ -817,15 +830,20 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
             int tap = 0, cc = 0;
             for (int ka = 0; ka < n_a; ++ka) {
-                if (!mbar_wait_warp(empty0 + 8 * s, ph ^ 1)) {
-                    if (lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
+                if (!mbar_wait_warp(empty0 + 8 * s, ph ^ 1, g.wait_limit)) {
+                    if (lane == 0) atomicExch(g.err, ERR_WAIT_EMPTY);
                     ok = false;
                     break;
                 }
                 const uint32_t fb = full0 + 8 * s;
+                // test switch: the bytes of this stage are announced but never copied
+                const bool stall = g.stall_first_load && ka == 0 && mt == 0 && blockIdx.y == 0;
                 if (elect_one()) {
                     const bool aux = AUX && ka == 0;
                     mbar_expect_tx(fb, g.a_bytes + (g.b_resident ? 0u : g.b_bytes) + (aux ? g.aux_bytes : 0u));
+                }
+                if (!stall && elect_one()) {
+                    const bool aux = AUX && ka == 0;
                     if (aux) tma_load_2d(smem_u32(sA + s * g.a_stage + g.aux_off), &map_xa, fb, 0, mt * 128);
                     if (MODE == 1) {
                         tma_load_2d(smem_u32(sA + s * g.a_stage), &map_a, fb, ka * CB, mt * 128 + g.blk_off);
@@ -844,14 +862,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 if (++s == S) { s = 0; ph ^= 1; }
             }
         }
-        // Every issued copy must have landed before the CTA exits.
+        // Every issued copy must have landed before the CTA exits (a stage that never
+        // completes is reported; the others are still waited for).
         for (int st = 0; st < S; ++st)
             if ((used >> st) & 1u)
-                if (!mbar_wait_warp(full0 + 8 * st, (last_ph >> st) & 1u)) {
-                    if (lane == 0) atomicExch(&g_ptq8_error, ERR_DRAIN);
-                    break;
-                }
-        if (g.b_resident && !mbar_wait_warp(bfull, 0) && lane == 0) atomicExch(&g_ptq8_error, ERR_DRAIN);
+                if (!mbar_wait_warp(full0 + 8 * st, (last_ph >> st) & 1u, g.wait_limit) && lane == 0)
+                    atomicExch(g.err, ERR_DRAIN);
+        if (g.b_resident && !mbar_wait_warp(bfull, 0, g.wait_limit) && lane == 0) atomicExch(g.err, ERR_DRAIN);
     } else if (warp == 1) {
         // ---------------- MMA issuer (whole warp; one elected lane issues each MMA)
         const uint32_t idesc = make_idesc_i8(BN);
@@ -865,22 +882,22 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const uint64_t b_chunk_step = static_cast<uint64_t>(sb_stride >> 4);
         const uint64_t xadesc0 = AUX ? make_sdesc(smem_u32(sA + g.aux_off), g.aux_kb) : 0;
         const uint64_t xbdesc = AUX ? make_sdesc(smem_u32(sBx), g.aux_kb) : 0;
-        bool ok = !g.b_resident || mbar_wait_warp(bfull, 0);
-        if (!ok && lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+        bool ok = !g.b_resident || mbar_wait_warp(bfull, 0, g.wait_limit);
+        if (!ok && lane == 0) atomicExch(g.err, ERR_WAIT_FULL);
         int s = 0;
         uint32_t ph = 0;
         int buf = 0;
         uint32_t use_ph = 0;   // parity of the current use of accumulator `buf`
         for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
-            if (!mbar_wait_warp(acce0 + 8 * buf, use_ph ^ 1u)) {
-                if (lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
+            if (!mbar_wait_warp(acce0 + 8 * buf, use_ph ^ 1u, g.wait_limit)) {
+                if (lane == 0) atomicExch(g.err, ERR_WAIT_EMPTY);
                 break;
             }
             tc_fence_after();
             const uint32_t d = tmem + static_cast<uint32_t>(buf * g.acc_cols);
             for (int ka = 0; ka < n_a; ++ka) {
-                if (!mbar_wait_warp(full0 + 8 * s, ph)) {
-                    if (lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+                if (!mbar_wait_warp(full0 + 8 * s, ph, g.wait_limit)) {
+                    if (lane == 0) atomicExch(g.err, ERR_WAIT_FULL);
                     ok = false;
                     break;
                 }
@@ -919,7 +936,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
         // all MMAs of this warp complete before TMEM can be released
         mma_commit_elect(donebar);
-        if (!mbar_wait_warp(donebar, 0) && lane == 0) atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
+        if (!mbar_wait_warp(donebar, 0, g.wait_limit) && lane == 0) atomicExch(g.err, ERR_WAIT_ACC);
     } else {
         // ---------------- epilogue: TMEM lanes 32*(warp%4) .. +31 = tile rows.
         // Warps form NG groups; group gi takes tiles t = gi (mod NG), held in accumulator
@@ -1008,8 +1025,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 position(mt, n, h, w, valid, pq, pf);
                 float res[16];
                 if (RES && !AUX && valid && active) load_res16(e, pf, ch, nv, res);
-                if (!mbar_wait(accf0 + 8 * buf, use & 1u)) {
-                    atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
+                if (!mbar_wait(accf0 + 8 * buf, use & 1u, g.wait_limit)) {
+                    atomicExch(g.err, ERR_WAIT_ACC);
                     break;
                 }
                 tc_fence_after();
@@ -1068,8 +1085,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 if (RES && !AUX && valid && slice < ncg && c0 < tile_end)
                     load_res16(e, pf, c0, min(16, tile_end - c0), res);
             }
-            if (!mbar_wait(accf0 + 8 * buf, use & 1u)) {
-                atomicExch(&g_ptq8_error, ERR_WAIT_ACC);
+            if (!mbar_wait(accf0 + 8 * buf, use & 1u, g.wait_limit)) {
+                atomicExch(g.err, ERR_WAIT_ACC);
                 break;
             }
             tc_fence_after();
@@ -1344,6 +1361,8 @@ struct DwGeom {
     int n_stages;
     int strips;       // strips per output row (OW / T)
     FastDiv fd_strips, fd_rs, fd_bands;   // strips, R * strips, bands
+    int* err;              // the engine's device error word
+    long long wait_limit;  // bounded-wait limit, clock cycles
 };
 
 constexpr int kDwMaxStages = 4;
@@ -1412,8 +1431,9 @@ __global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const in
         for (uint32_t u = blockIdx.x; u < static_cast<uint32_t>(d.n_units); u += gridDim.x, ++issued) {
             const int stage = issued % d.n_stages;
             if (issued >= d.n_stages &&
-                !mbar_wait(bar0 + 8 * (kDwMaxStages + stage), static_cast<uint32_t>(issued / d.n_stages - 1) & 1u)) {
-                atomicExch(&g_ptq8_error, ERR_WAIT_EMPTY);
+                !mbar_wait(bar0 + 8 * (kDwMaxStages + stage), static_cast<uint32_t>(issued / d.n_stages - 1) & 1u,
+                           d.wait_limit)) {
+                atomicExch(d.err, ERR_WAIT_EMPTY);
                 break;
             }
             int n0, r0, k;
@@ -1429,10 +1449,8 @@ __global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const in
         // let the copies issued last land before the CTA's shared memory goes away
         // (already complete unless a consumer gave up early)
         for (int j = max(0, issued - d.n_stages); j < issued; ++j)
-            if (!mbar_wait(bar0 + 8 * (j % d.n_stages), static_cast<uint32_t>(j / d.n_stages) & 1u)) {
-                atomicExch(&g_ptq8_error, ERR_DRAIN);
-                break;
-            }
+            if (!mbar_wait(bar0 + 8 * (j % d.n_stages), static_cast<uint32_t>(j / d.n_stages) & 1u, d.wait_limit))
+                atomicExch(d.err, ERR_DRAIN);
         return;
     }
 
@@ -1465,8 +1483,8 @@ __global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const in
     int it = 0;
     for (uint32_t u = blockIdx.x; u < static_cast<uint32_t>(d.n_units); u += gridDim.x, ++it) {
         const int stage = it % d.n_stages;
-        if (!mbar_wait_warp(bar0 + 8 * stage, static_cast<uint32_t>(it / d.n_stages) & 1u)) {
-            if ((threadIdx.x & 31) == 0) atomicExch(&g_ptq8_error, ERR_WAIT_FULL);
+        if (!mbar_wait_warp(bar0 + 8 * stage, static_cast<uint32_t>(it / d.n_stages) & 1u, d.wait_limit)) {
+            if ((threadIdx.x & 31) == 0) atomicExch(d.err, ERR_WAIT_FULL);
             break;
         }
         int n0, r0, k;

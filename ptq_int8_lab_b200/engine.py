@@ -42,7 +42,8 @@ EXPORTS = (
     "ptq8_engine_set_act_mode", "ptq8_engine_set_calib", "ptq8_engine_set_input_shape",
     "ptq8_engine_alloc_scratch", "ptq8_engine_set_stream", "ptq8_engine_set_max_ctas", "ptq8_engine_stream", "ptq8_engine_forward",
     "ptq8_engine_forward_device", "ptq8_engine_forward_async", "ptq8_engine_input_buffer", "ptq8_engine_logits_buffer", "ptq8_engine_run", "ptq8_engine_copy_logits",
-    "ptq8_engine_sync", "ptq8_engine_check_device_error", "ptq8_engine_tensor_info", "ptq8_engine_dump",
+    "ptq8_engine_sync", "ptq8_engine_check_device_error", "ptq8_engine_set_wait_test", "ptq8_engine_tensor_info",
+    "ptq8_engine_dump", "ptq8_engine_dump_range",
     "ptq8_engine_n_launches", "ptq8_engine_passes_log", "ptq8_engine_profile",
     "ptq8_load", "ptq8_forward", "ptq8_forward_debug", "ptq8_capture_graph", "ptq8_destroy", "ptq8_last_error",
 )
@@ -109,8 +110,10 @@ def lib() -> ctypes.CDLL:
         "ptq8_engine_copy_logits": (c_int, [c_void_p, c_int, c_void_p]),
         "ptq8_engine_sync": (c_int, [c_void_p]),
         "ptq8_engine_check_device_error": (c_int, [c_void_p]),
+        "ptq8_engine_set_wait_test": (c_int, [c_void_p, ctypes.c_longlong, c_int]),
         "ptq8_engine_tensor_info": (c_int, [c_void_p, c_int, c_int, P(c_int)]),
         "ptq8_engine_dump": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_size]),
+        "ptq8_engine_dump_range": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size]),
         "ptq8_engine_n_launches": (c_int, [c_void_p]),
         "ptq8_engine_profile": (c_int, [c_void_p, c_int, c_int, P(ctypes.c_float), P(ctypes.c_double),
                                         P(ctypes.c_double), P(c_int), c_int, P(c_int)]),
@@ -352,24 +355,57 @@ class Int8Engine:
         self._check(lib().ptq8_engine_tensor_info(self._h, what, index, s))
         return tuple(s)
 
-    def dump_codes(self, conv: int, n: int) -> np.ndarray:
-        """int8 input codes of conv `conv` after the last forward: NHWC (stem: im2col rows)."""
+    def dump_codes(self, conv: int, n: int, n0: int = 0) -> np.ndarray:
+        """int8 input codes of conv `conv` for images [n0, n0+n) of the last forward: NHWC
+        (stem: im2col rows)."""
         _, h, w, ld = self.tensor_info(0, conv)
         out = np.empty((n, h, w, ld), dtype=np.int8)
-        self._check(lib().ptq8_engine_dump(self._h, 0, conv, n, out.ctypes.data, out.nbytes))
+        self._check(lib().ptq8_engine_dump_range(self._h, 0, conv, n0, n, out.ctypes.data, out.nbytes))
         return out
 
-    def dump_final(self, n: int) -> np.ndarray:
-        """fp32 map fed to the pooling head after the last forward, NHWC."""
+    def dump_final(self, n: int, n0: int = 0) -> np.ndarray:
+        """fp32 map fed to the pooling head for images [n0, n0+n) of the last forward, NHWC."""
         _, h, w, c = self.tensor_info(1)
         out = np.empty((n, h, w, c), dtype=np.float32)
-        self._check(lib().ptq8_engine_dump(self._h, 1, 0, n, out.ctypes.data, out.nbytes))
+        self._check(lib().ptq8_engine_dump_range(self._h, 1, 0, n0, n, out.ctypes.data, out.nbytes))
         return out
+
+    def check_device_error(self):
+        """Raise Ptq8Error (status PTQ8_ERR_TIMEOUT) if a bounded device wait ran out."""
+        self._check(lib().ptq8_engine_check_device_error(self._h))
+
+    def set_wait_test(self, wait_limit_cycles: int = 0, stall_first_load: bool = False):
+        """Failure-detection test hook (see ptq8_engine_set_wait_test)."""
+        self._check(lib().ptq8_engine_set_wait_test(self._h, int(wait_limit_cycles), 1 if stall_first_load else 0))
 
     def __del__(self):
         h, self._h = getattr(self, "_h", None), None
         if h and _lib is not None:
-            _lib.ptq8_engine_destroy(h)
+            if getattr(self, "_one_call", False):
+                _lib.ptq8_destroy(h)
+            else:
+                _lib.ptq8_engine_destroy(h)
+
+
+def load_one_call(model_path, calib_path, plan_path=None, max_batch: int = 0, device: int = 0, w_bits: int = 8,
+                  act_mode: int = ACT_ABSMAX, passes: int = 0) -> Int8Engine:
+    """The one-call interface: ptq8_load (model + PTQC + layer plan + build + calib +
+    scratch in one call; the engine owns its model), wrapped as an Int8Engine."""
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(1024)
+    opts = Opts(device, w_bits, 8, act_mode, passes, max_batch)
+    rc = lib().ptq8_load(str(model_path).encode(), str(calib_path).encode(),
+                         str(plan_path).encode() if plan_path else None, ctypes.byref(opts), ctypes.byref(h), err,
+                         len(err))
+    if rc:
+        raise Ptq8Error(err.value.decode(errors="replace"), rc)
+    e = Int8Engine.__new__(Int8Engine)
+    e._h = h.value
+    e._one_call = True
+    e.device = device
+    e.model = Model.load(model_path)   # shape metadata (fc_out) for forward()
+    e.max_batch = max_batch
+    return e
 
 
 def open_engine(model_path, calib_path, plan_path=None, max_batch: int = 256, device: int = 0,

@@ -20,11 +20,24 @@ def stem_rows(codes_nchw: np.ndarray, conv: O.Conv, kpad: int) -> np.ndarray:
     return out
 
 
-def compare(engine, trace: O.Trace, model: O.Model, n: int, logits: np.ndarray, rtol: float = 1e-5):
-    """Assert bit-exact int8 conv-input codes and final fp32 map; logits within rtol."""
+def _dump_images(dump, images):
+    """dump(n, n0) for each engine image in `images` (any order), stacked."""
+    return np.concatenate([dump(1, int(k)) for k in images], axis=0)
+
+
+def compare(engine, trace: O.Trace, model: O.Model, n: int, logits: np.ndarray, rtol: float = 1e-5,
+            images=None):
+    """Assert bit-exact int8 conv-input codes and final fp32 map; logits within rtol.
+
+    `images` (optional): the engine batch positions of the trace's n images (trace row k is
+    engine image images[k]), for checks of a few images of a large batch; `logits` are then
+    the engine logits of those images."""
     bad = []
     for i, conv in enumerate(model.convs):
-        got = engine.dump_codes(i, n)
+        if images is None:
+            got = engine.dump_codes(i, n)
+        else:
+            got = _dump_images(lambda c, k: engine.dump_codes(i, c, k), images)
         want = trace.codes[i]
         if i == model.stem:
             exp = stem_rows(want, conv, got.shape[-1])
@@ -45,7 +58,7 @@ def compare(engine, trace: O.Trace, model: O.Model, n: int, logits: np.ndarray, 
         if not ok:
             bad.append((i, -1, -1, got.size))
     assert not bad, f"int8 code mismatches (conv, n_diff, max|diff|, size): {bad}"
-    fin = engine.dump_final(n)
+    fin = engine.dump_final(n) if images is None else _dump_images(engine.dump_final, images)
     want = trace.block_out[-1].transpose(0, 2, 3, 1) if trace.block_out else trace.stem_out.transpose(0, 2, 3, 1)
     assert np.array_equal(fin, want), f"final fp32 map differs: max|diff|={np.abs(fin - want).max()}"
     ok, err = O.logits_close(logits, trace.logits, rtol)

@@ -46,6 +46,28 @@ def test_rejects_size_beyond_scratch():
     assert b"exceeds the fixed scratch" in err.value
 
 
+@pytest.mark.parametrize("lo,hi,mode,needle", [
+    (2.0, 1.0, 1, b"lo > hi"),                     # MinMax with an inverted range
+    (2.0, 1.0, 0, b"lo > hi"),
+    (-np.inf, 1.0, 0, b"not finite"),
+    (-1.0, np.inf, 1, b"not finite"),
+    (np.nan, 1.0, 0, b"not finite"),
+    (np.nan, np.nan, 1, b"not finite"),
+    (-1.0, 1.0, 2, b"act mode 2"),
+    (-1.0, 1.0, -1, b"act mode -1"),
+])
+def test_rejects_bad_range_or_mode_before_device_work(lo, hi, mode, needle):
+    """Checked before any CUDA call (these run without a GPU): an infinite or NaN scale
+    would otherwise leave the host-side multiplier search without an exit."""
+    x = np.zeros(64, dtype=np.float32)
+    out = np.empty(x.size, dtype=np.int8)
+    err = ctypes.create_string_buffer(512)
+    rc = E.lib().ptq8_quantize_device_noalloc(0, _f(x), x.size, lo, hi, mode, _q(out), err, len(err))
+    assert rc == 1, err.value
+    assert needle in err.value
+    assert E.lib().ptq8_quantize_device(0, _f(x), x.size, lo, hi, mode, _q(out)) == 1
+
+
 @pytest.mark.gpu
 def test_matches_existing_entry_on_two_calls():
     rng = np.random.default_rng(11)
