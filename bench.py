@@ -56,7 +56,8 @@ def parse():
                     help="BASELINE config (4: the headline ResNet-18 W8A8 at 8192 images per GPU)")
     ap.add_argument("--batch", type=int, default=None, help="images per GPU (default: the config's batch)")
     ap.add_argument("--model-cache", default=os.environ.get("PTQ8_MODEL_CACHE", "/tmp/ptq8_models"))
-    ap.add_argument("--cpu-sample", type=int, default=12, help="images in the timed CPU-baseline sample")
+    ap.add_argument("--cpu-sample", type=int, default=6,
+                    help="images in the timed CPU-baseline sample (about 8 s per run at the reference's rate)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -85,6 +86,25 @@ def model_files(cache: str, rank: int, world: int, barrier, cfg: int = 4):
         marker.write_text(json.dumps({k: str(p[k]) for k in ("model", "calib", "plan")}))
     barrier()
     return json.loads(marker.read_text())
+
+
+def gather_logits(gathered, local):
+    """The multi-GPU step's one collective: every rank's fp32 logits [B, 10], concatenated
+    in rank order into `gathered` [world * B, 10] on every rank."""
+    import torch.distributed as dist
+    dist.all_gather_into_tensor(gathered, local)
+
+
+def all_ranks(x: float, device) -> list:
+    """x of every rank, in rank order ([x] without a process group)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [x]
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    out = torch.empty(dist.get_world_size(), dtype=torch.float64, device=device)
+    dist.all_gather_into_tensor(out, t)
+    return [float(v) for v in out.cpu()]
 
 
 def max_over_ranks(x: float, device) -> float:
@@ -135,7 +155,8 @@ class ClockSampler:
         except ValueError:
             return None
 
-    def stop(self, t0: float, t1: float) -> dict:
+    def stop(self, windows) -> dict:
+        """Summary of the samples taken inside the timed windows [(t0, t1), ...]."""
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
@@ -152,8 +173,9 @@ class ClockSampler:
         os.unlink(self.f.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        inside = [r for r in rows if t0 <= self._ts(r[0]) <= t1]
+        inside = [r for r in rows if any(t0 <= self._ts(r[0]) <= t1 for t0, t1 in windows)]
         if not inside:
+            t0, t1 = windows[0]
             before = [r for r in rows if self._ts(r[0]) < t0][-1:]
             after = [r for r in rows if self._ts(r[0]) > t1][:1]
             inside = before + after
@@ -209,27 +231,38 @@ def cpu_baseline(paths, n_img: int, seed: int = 99, runs: int = 3) -> dict:
         O.MATMUL_MODE["mode"] = "blas"
     dt = sorted(dts)[len(dts) // 2]
     return {"value": n_img / dt, "unit": "images/s", "cores": 1, "kind": "port",
-            "sample": f"{n_img} images of the same workload, numpy int32 matmul (06-gpu-int8/cpp/ref_e2e.py:180), "
-                      f"median of {runs} runs ({', '.join(f'{t:.2f}' for t in dts)} s) after a warm-up",
+            "sample": f"{n_img} images of the same workload, numpy int32 matmul with the reference's weight layout "
+                      f"(06-gpu-int8/cpp/ref_e2e.py:180,213-218; times within 1% of ref_e2e.forward, "
+                      f"profiles/cpu_baseline_port_vs_ref_e2e.md), median of {runs} runs "
+                      f"({', '.join(f'{t:.2f}' for t in dts)} s) after a warm-up",
             **host_cpu()}
 
 
-def _ref_worker(args):
-    model, calib, plan, n_img, seed = args
-    import numpy as np
+_REF_ORACLE = None
+
+
+def _ref_init(model, calib, plan):
+    """Pool initializer: each worker process loads the model and quantizes its weights once
+    (the reference's forward does this before its timed loop, ref_e2e.py:210-219)."""
+    global _REF_ORACLE
     from oracle import ptq8_oracle as O
     from ptq_int8_lab_b200 import modelgen as mg
     O.MATMUL_MODE["mode"] = "int32"
-    m = O.read_model(model)
-    orc = O.Oracle(m, O.read_ptqc(calib), layer_bits=mg.read_layer_plan(plan))
+    _REF_ORACLE = O.Oracle(O.read_model(model), O.read_ptqc(calib), layer_bits=mg.read_layer_plan(plan))
+
+
+def _ref_worker(args):
+    n_img, seed = args
+    import numpy as np
     x = np.random.default_rng(seed).standard_normal((n_img, 3, 32, 32)).astype(np.float32)
     t0 = time.perf_counter()
-    orc.forward(x, trace=False)
+    _REF_ORACLE.forward(x, trace=False)
     return time.perf_counter() - t0
 
 
 def run_reference(a):
-    """Reference arm: the reference's CPU integer forward, all host cores, bounded sample per step."""
+    """Reference arm: the reference's CPU integer forward (the bit-pinned port, with the
+    reference's GEMM layout and speed) on all host cores, a bounded sample per step."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
@@ -237,16 +270,15 @@ def run_reference(a):
     info = config_info(a.config)
     paths = model_files(a.model_cache, 0, 1, lambda: None, a.config)
     cores = os.cpu_count() or 1
-    per = 2
+    per = 1
     ctx = mp.get_context("spawn")
-    with ctx.Pool(cores) as pool:
-        for _ in range(max(a.warmup, 1) if a.warmup else 0):
-            pool.map(_ref_worker, [(paths["model"], paths["calib"], paths["plan"], 1, 7 + i) for i in range(cores)])
+    with ctx.Pool(cores, initializer=_ref_init, initargs=(paths["model"], paths["calib"], paths["plan"])) as pool:
+        for w in range(max(a.warmup, 1)):
+            pool.map(_ref_worker, [(1, 7 + 1000 * w + i) for i in range(cores)])
         times = []
         for s in range(a.steps):
             t0 = time.perf_counter()
-            pool.map(_ref_worker, [(paths["model"], paths["calib"], paths["plan"], per, 100 * s + i)
-                                   for i in range(cores)])
+            pool.map(_ref_worker, [(per, 100 * s + i) for i in range(cores)])
             times.append(time.perf_counter() - t0)
     imgs = per * cores * a.steps
     tot = sum(times)
@@ -255,10 +287,12 @@ def run_reference(a):
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tot / a.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"{info['name']} (BASELINE configs[{a.config}] shapes)", "batch_per_step": per * cores,
-                       "note": "bounded sample per step on host cores"},
+                       "note": "bounded sample per step on host cores; the CPU arm cannot run the GPU batch"},
             "cpu_baseline": {"value": v, "unit": "images/s", "cores": cores, "kind": "port",
-                             "sample": f"{per} images per process x {cores} spawn processes per step, "
-                                       f"numpy int32 matmul as ref_e2e.py:180", **host_cpu()},
+                             "sample": f"{per} image per process x {cores} spawn processes per step, model loaded "
+                                       f"once per process; numpy int32 matmul with the reference's weight layout "
+                                       f"(ref_e2e.py:180,213-218), timed within 1% of ref_e2e.forward "
+                                       f"(profiles/cpu_baseline_port_vs_ref_e2e.md)", **host_cpu()},
             "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -294,37 +328,73 @@ def main():
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     x = torch.randn(B, 3, 32, 32, device="cuda", generator=g, dtype=torch.float32)
     logits = torch.empty(B, 10, device="cuda", dtype=torch.float32)
-    gathered = torch.empty(world * B, 10, device="cuda", dtype=torch.float32) if world > 1 else None
     eng.forward_device(x.data_ptr(), B, logits.data_ptr())   # stage the input in the engine buffer
 
-    def step():
+    # N > 1: step k's logits go to buffer k % 2 on the engine stream; the all-gather runs on a
+    # side stream once they are there, so the next forward does not wait for the collective.
+    # The engine stream only waits for the gather two steps back (it read the same buffer).
+    comm = torch.cuda.Stream() if world > 1 else None
+    lbuf = [torch.empty(B, 10, device="cuda", dtype=torch.float32) for _ in range(2)]
+    gbuf = [torch.empty(world * B, 10, device="cuda", dtype=torch.float32) for _ in range(2)] if world > 1 else None
+    ev_ready = [torch.cuda.Event() for _ in range(2)]
+    ev_read = [torch.cuda.Event() for _ in range(2)]
+
+    def step(k: int):
         eng.run(B)
         if world > 1:
-            eng.copy_logits(B, logits.data_ptr())          # same stream as the collective
-            dist.all_gather_into_tensor(gathered, logits)
+            i = k & 1
+            stream.wait_event(ev_read[i])
+            eng.copy_logits(B, lbuf[i].data_ptr())
+            ev_ready[i].record(stream)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev_ready[i])
+                gather_logits(gbuf[i], lbuf[i])
+                ev_read[i].record(comm)
 
     clocks = ClockSampler(local)
     clocks.start()
-    for _ in range(a.warmup):
-        step()
+    for k in range(a.warmup):
+        step(k)
     torch.cuda.synchronize()
     eng.sync()
     barrier()
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
+    ev_fwd = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     t_wall0 = time.time()
     ev0.record(stream)
-    for _ in range(a.steps):
-        step()
+    for k in range(a.steps):
+        step(k)
+    ev_fwd.record(stream)          # this rank's forwards (and logits copies) are done
+    if comm is not None:
+        stream.wait_stream(comm)   # ... and every gather
     ev1.record(stream)
     torch.cuda.synchronize()
-    clk = clocks.stop(t_wall0, time.time())
-    ms = ev0.elapsed_time(ev1)
+    t_wall1 = time.time()
+    ms_local = ev0.elapsed_time(ev1)
+    fwd_ms_by_rank = [v / a.steps for v in all_ranks(ev0.elapsed_time(ev_fwd), "cuda")]
     eng.sync()
-    ms = max_over_ranks(ms, "cuda")
+    ms = max_over_ranks(ms_local, "cuda")
     ms_per_step = ms / a.steps
     value = world * B * a.steps / (ms / 1e3)
+    multi = None
+    if world > 1:
+        # the gather's own device time (comm stream, after the timed region), max over ranks
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        g0.record(comm)
+        for _ in range(10):
+            with torch.cuda.stream(comm):
+                gather_logits(gbuf[0], lbuf[0])
+        g1.record(comm)
+        torch.cuda.synchronize()
+        multi = {"gather_ms": max_over_ranks(g0.elapsed_time(g1) / 10, "cuda"),
+                 "gather_bytes_per_rank": B * 10 * 4,
+                 "forward_ms_per_step_by_rank": fwd_ms_by_rank,
+                 "rank_spread_ms_per_step": max(fwd_ms_by_rank) - min(fwd_ms_by_rank),
+                 "gather": "NCCL all_gather of fp32 logits on a side stream, double-buffered; "
+                           "the timed region ends after the last gather"}
 
     # ---- per-launch profile (device events per step) -> roofline of the dense convs
     prof = eng.profile(B, iters=3)
@@ -349,11 +419,19 @@ def main():
         for line in tp.read_text().splitlines():
             if line.startswith("traffic_bytes_per_forward_b8192 ="):
                 traffic = int(line.split("=")[1].strip())
+    # Second denominator: the kind::i8 MMA issue rate measured on this pool (N >= 128 shapes:
+    # 8192 MAC per clock per SM) at the median SM clock of the timed region.
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
     roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
                 "frac": achieved / int8_peak, "traffic": traffic,
                 "kernel": "conv_tc_kernel (all dense convs of one forward)",
                 "peak_source": f"2 x bf16_tflops of {src} MEASURED_PEAKS.json",
-                "dense_conv_ms": tc_ms, "forward_ms_sum_of_launches": sum(p["ms"] for p in prof)}
+                "dense_conv_ms": tc_ms, "forward_ms_sum_of_launches": sum(p["ms"] for p in prof),
+                "per_launch": [{"step": p["step"], "kind": "stem" if p["kind"] == 0 else "conv",
+                                "ms": p["ms"], "tops": 2.0 * p["macs"] / (p["ms"] / 1e3) / 1e12,
+                                "frac": 2.0 * p["macs"] / (p["ms"] / 1e3) / 1e12 / int8_peak}
+                               for p in tc if p["ms"] > 0]}
+    wb = eng.weight_bytes()
 
     # ---- end to end through the C-ABI host-buffer forwards (H2D + graph + D2H every step).
     # Headline: ptq8_engine_forward_async, the pipelined call (step k+1's H2D overlaps step
@@ -363,6 +441,8 @@ def main():
     xh.copy_(x.cpu())
     lh = torch.empty(B, 10, dtype=torch.float32, pin_memory=True)
 
+    windows = [(t_wall0, t_wall1)]   # host-time windows of the timed regions (clock samples)
+
     def host_loop(pipelined: bool) -> float:
         for _ in range(2):
             eng.forward_host_ptr(xh.data_ptr(), B, 3, 32, 32, lh.data_ptr())
@@ -371,6 +451,7 @@ def main():
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         barrier()
+        w0 = time.time()
         e0.record(stream)
         for _ in range(a.steps):
             if pipelined:
@@ -380,10 +461,16 @@ def main():
         eng.sync()
         e1.record(stream)
         torch.cuda.synchronize()
+        windows.append((w0, time.time()))
         return max_over_ranks(e0.elapsed_time(e1), "cuda")
 
     ems = host_loop(True)
     ems_sync = host_loop(False)
+    clk = clocks.stop(windows)
+    clk["windows"] = "the device-timed loop and both e2e loops"
+    roofline["peak_i8_issue_rate"] = (8192 * sms * clk["sm_mhz"] * 1e6 * 2 / 1e12) if clk.get("sm_mhz") else None
+    if roofline["peak_i8_issue_rate"]:
+        roofline["frac_of_i8_issue_rate"] = achieved / roofline["peak_i8_issue_rate"]
     e2e = {"value": world * B * a.steps / (ems / 1e3), "unit": "images/s",
            "h2d_bytes_per_step": B * 3 * 32 * 32 * 4, "d2h_bytes_per_step": B * 10 * 4,
            "call": "ptq8_engine_forward_async (pinned host buffers; step k+1's H2D overlaps step k's forward)",
@@ -395,9 +482,11 @@ def main():
                 "vs_baseline": None, "dtype": "int8", "data": "synthetic",
                 "config": {"workload": f"{info['name']}_b{B} (BASELINE configs[{a.config}])", "batch_per_gpu": B,
                            "parallelism": f"dp{world}", "l2": "inputs and activations larger than L2 (>10 GB/step)",
-                           "logits_gather": "nccl all_gather per step" if world > 1 else "none"},
-                "roofline": roofline, "e2e": e2e, "clocks": clk,
+                           "logits_gather": "nccl all_gather per step (side stream)" if world > 1 else "none"},
+                "roofline": roofline, "e2e": e2e, "clocks": clk, "weights": wb,
                 "gpu_launches": a.steps * eng.n_launches()}
+        if multi is not None:
+            line["multi_gpu"] = multi
         if not a.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(paths, a.cpu_sample)
         print(json.dumps(line), flush=True)

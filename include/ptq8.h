@@ -190,6 +190,13 @@ int ptq8_engine_profile(ptq8_engine* e, int n, int iters, float* ms, double* mac
                         int cap, int* n_steps);
 /* Number of kernel launches in one forward (the CUDA graph's kernel nodes). */
 int ptq8_engine_n_launches(const ptq8_engine* e);
+/* Conv weight bytes the planned engine keeps in device memory, the bytes the same
+ * weights take as int8 codes, and how many convs hold W4 codes packed two per byte
+ * (W4 convs whose weight slab stays resident in shared memory, and depthwise W4
+ * tables).  No counterpart in the reference, whose PTQ2 stores W4 layers as fp32 QDQ
+ * values (09-ptq-toolkit/ptq_toolkit/pipeline.py:272-279) and whose engine holds
+ * every code as a byte (int8_engine.cuh:211-276). */
+int ptq8_engine_weight_bytes(const ptq8_engine* e, size_t* device_bytes, size_t* int8_bytes, int* packed_convs);
 /* Human-readable record of what the graph passes did. */
 int ptq8_engine_passes_log(const ptq8_engine* e, char* out, size_t cap);
 

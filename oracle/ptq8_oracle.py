@@ -104,15 +104,25 @@ def apply_activation(y: np.ndarray, act: int) -> np.ndarray:
 
 
 # "blas": exact float64 BLAS product (fast, used by the parity tests);
-# "int32": numpy int32 matmul exactly as 06-gpu-int8/cpp/ref_e2e.py:180 does it
-# (single-threaded, used as the timed CPU baseline of the reference's algorithm).
+# "int32": numpy int32 matmul exactly as 06-gpu-int8/cpp/ref_e2e.py:180 does it, with
+# the weights as the reference lays them out (a row-major (Kpad, Cout) matrix, K padded
+# to a multiple of 8, ref_e2e.py:213-218) -- numpy's integer matmul has no BLAS path, so
+# its speed depends on that layout; single-threaded, used as the timed CPU baseline of
+# the reference's algorithm.
 MATMUL_MODE = {"mode": "blas"}
 
 
 def int_matmul(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     """Exact int32 product of small-integer matrices."""
     if MATMUL_MODE["mode"] == "int32":
-        return np.asarray(a, dtype=np.int32) @ np.asarray(b, dtype=np.int32)
+        k = a.shape[1]
+        kpad = (k + 7) // 8 * 8
+        a32 = np.asarray(a, dtype=np.int32)
+        if kpad != k:   # the reference's im2col writes zero columns up to Kpad (ref_e2e.py:152-155)
+            a32 = np.concatenate([a32, np.zeros((a32.shape[0], kpad - k), dtype=np.int32)], axis=1)
+        bt = np.zeros((kpad, b.shape[1]), dtype=np.int8)
+        bt[:k] = b
+        return a32 @ bt.astype(np.int32)
     r = np.asarray(a, dtype=np.float64) @ np.asarray(b, dtype=np.float64)
     if r.size and (np.abs(r).max() >= 2 ** 31):
         raise OverflowError("int32 accumulator overflow")

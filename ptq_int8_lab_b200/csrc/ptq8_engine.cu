@@ -105,6 +105,9 @@ struct Step {
     double s_in = 1.0;
     // device parameters
     int8_t* d_w = nullptr;
+    uint8_t* d_w4 = nullptr;    // W4 codes two per byte (resident-slab tensor-core convs), else null
+    bool w_packed = false;      // d_w4 (tensor-core) / a packed d_dwt table (depthwise) holds the weights
+    size_t w_dev_bytes = 0;     // bytes of this step's weights in device memory
     float* d_factor = nullptr;
     float* d_bias = nullptr;
     std::vector<float> h_factor, h_bias;   // host copies (tensor-core convs take them as kernel parameters)
@@ -836,8 +839,22 @@ int finalize(ptq8_engine* e, int max_batch) {
                 for (int o = 0; o < c.cout; ++o)
                     for (int j = 0; j < 3; ++j)
                         t[(size_t)(o / 4) * 12 + 4 * j + o % 4] = code(o, j) | code(o, 3 + j) << 8 | code(o, 6 + j) << 16;
-                if (!e->dalloc(&st.d_dwt, t.size() * 4, "alloc dw table")) return PTQ8_ERR_CUDA;
-                cudaMemcpy(st.d_dwt, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+                if (cq.bits == 4) {
+                    // W4: each word as 16 bits, its three codes in nibbles 0-2 (24 bytes per group)
+                    std::vector<uint16_t> h(t.size());
+                    for (size_t k = 0; k < t.size(); ++k)
+                        h[k] = (uint16_t)((t[k] & 0xF) | ((t[k] >> 4) & 0xF0) | ((t[k] >> 8) & 0xF00));
+                    if (!e->dalloc(&st.d_dwt, h.size() * 2, "alloc dw table")) return PTQ8_ERR_CUDA;
+                    cudaMemcpy(st.d_dwt, h.data(), h.size() * 2, cudaMemcpyHostToDevice);
+                    st.w_packed = true;
+                    st.w_dev_bytes = h.size() * 2;
+                } else {
+                    if (!e->dalloc(&st.d_dwt, t.size() * 4, "alloc dw table")) return PTQ8_ERR_CUDA;
+                    cudaMemcpy(st.d_dwt, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+                    st.w_dev_bytes = t.size() * 4;
+                }
+            } else {
+                st.w_dev_bytes = w.size();
             }
             continue;
         }
@@ -876,17 +893,11 @@ int finalize(ptq8_engine* e, int max_batch) {
             return e->fail(strf("conv[%d]: %d output channels exceed the kernel's %d", st.conv, c.cout, kMaxConstCh));
         if (st.n_ntiles > 1 && st.bn % 32 != 0)
             return e->fail(strf("conv[%d]: N tile %d breaks the 32-byte store alignment", st.conv, st.bn));
-        if (!e->dalloc(&st.d_w, w.size(), "alloc weights")) return PTQ8_ERR_CUDA;
-        cudaMemcpy(st.d_w, w.data(), w.size(), cudaMemcpyHostToDevice);
-        if (st.fused) continue;   // weights and constants are read by the conv that computes it
-        {
-            cuuint64_t dims[2] = {(cuuint64_t)st.ktot, (cuuint64_t)c.cout};
-            cuuint64_t strides[1] = {(cuuint64_t)st.ktot};
-            cuuint32_t box[2] = {(cuuint32_t)st.cb, (cuuint32_t)st.bn};
-            cuuint32_t estr[2] = {1, 1};
-            if (!make_map(e, &st.map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, st.d_w, dims, strides, box, estr,
-                          swizzle_for(st.cb)))
-                return PTQ8_ERR_CUDA;
+        if (st.fused) {   // weights and constants are read (as int8, by TMA) by the conv that computes it
+            if (!e->dalloc(&st.d_w, w.size(), "alloc weights")) return PTQ8_ERR_CUDA;
+            cudaMemcpy(st.d_w, w.data(), w.size(), cudaMemcpyHostToDevice);
+            st.w_dev_bytes = w.size();
+            continue;
         }
         tile_shape(max_batch, st.oh, st.ow, &st.TW, &st.TH, &st.TN);
         st.n_kchunks = st.kind == K_STEM_IM2COL ? st.kpad / st.cb : st.kh * st.kw * (cpad / st.cb);
@@ -917,6 +928,29 @@ int finalize(ptq8_engine* e, int max_batch) {
         }
         if (st.smem > kSmemBudget)
             return e->fail(strf("conv[%d]: no pipeline fits in shared memory", st.conv));
+        // Weights in HBM: W4 codes of a resident slab two per byte (unpacked into shared memory
+        // by the kernel); otherwise the int8 matrix, loaded by TMA.  The stem's weights stay
+        // int8: layer1.0.conv2's aux GEMM reads them with TMA.
+        st.w_packed = cq.bits == 4 && st.kind == K_TC && st.b_resident;
+        if (st.w_packed) {
+            std::vector<uint8_t> p(w.size() / 2);
+            for (size_t k = 0; k < p.size(); ++k)
+                p[k] = (uint8_t)((w[2 * k] & 0x0F) | ((w[2 * k + 1] & 0x0F) << 4));
+            if (!e->dalloc(&st.d_w4, p.size(), "alloc packed weights")) return PTQ8_ERR_CUDA;
+            cudaMemcpy(st.d_w4, p.data(), p.size(), cudaMemcpyHostToDevice);
+            st.w_dev_bytes = p.size();
+        } else {
+            if (!e->dalloc(&st.d_w, w.size(), "alloc weights")) return PTQ8_ERR_CUDA;
+            cudaMemcpy(st.d_w, w.data(), w.size(), cudaMemcpyHostToDevice);
+            st.w_dev_bytes = w.size();
+            cuuint64_t dims[2] = {(cuuint64_t)st.ktot, (cuuint64_t)c.cout};
+            cuuint64_t strides[1] = {(cuuint64_t)st.ktot};
+            cuuint32_t box[2] = {(cuuint32_t)st.cb, (cuuint32_t)st.bn};
+            cuuint32_t estr[2] = {1, 1};
+            if (!make_map(e, &st.map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, st.d_w, dims, strides, box, estr,
+                          swizzle_for(st.cb)))
+                return PTQ8_ERR_CUDA;
+        }
         if (st.kind == K_STEM_IM2COL) {
             // the im2col rows form a bordered [N][OH+2][OW+2][kpad] map read as a 1x1 conv
             const cuuint64_t hp = st.oh + 2, wp = st.ow + 2;
@@ -1021,6 +1055,8 @@ int finalize(ptq8_engine* e, int max_batch) {
             if (st.kind != K_DW || !st.d_dwt) continue;
             if (!plan_dw3x3(e, st, max_batch)) {
                 st.d_dwt = nullptr;   // no tiling fits: the generic depthwise kernel runs it
+                st.w_packed = false;  // (with its int8 weights)
+                st.w_dev_bytes = (size_t)st.kh * st.kw * st.oc;
                 continue;
             }
             if (!e->cuda_ok(cudaFuncSetAttribute(st.dw_kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kDwSmemLimit),
@@ -1142,6 +1178,7 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         d.fd_bands = make_fastdiv(d.bands);
         d.err = e->d_err;
         d.wait_limit = e->wait_limit;
+        d.w_packed = st.w_packed ? 1 : 0;
         const int grid = std::max(1, std::min(d.n_units, st.dw_ctas));
         launch_pdl((DwKernel)st.dw_kfn, dim3(grid), dim3(st.dw_cons + 32), (size_t)d.n_stages * d.stage_bytes, s,
                    vin.codes[vin.code_index(st.s_in)], (const uint4*)st.d_dwt, d, ep);
@@ -1221,6 +1258,10 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
     g.b_bytes = (uint32_t)(st.bn * st.cb);
     g.err = e->d_err;
     g.wait_limit = e->wait_limit;
+    g.w4 = st.d_w4;
+    g.w4_ld = st.ktot / 2;
+    g.w_rows = e->q[st.conv].spec.cout;
+    g.b_packed = st.w_packed ? 1 : 0;
     g.stall_first_load = 0;
     if (e->stall_first_load) {   // the forward's first tensor-core conv only
         size_t first = e->steps.size();
@@ -1293,7 +1334,8 @@ void step_work(const ptq8_engine* e, int n, size_t si, double* macs, double* byt
     *macs = pos * c.cout * (double)c.cin * c.kh * c.kw;
     const double inb = st.kind == K_STEM_IM2COL ? (double)n * st.ih * st.iw * st.ic * 4.0
                                                 : (double)n * st.ih * st.iw * st.ic;
-    *bytes = inb + (double)c.cout * c.cin * c.kh * c.kw + outb + resb;
+    // weights once: W4 codes held two per byte count half a byte each
+    *bytes = inb + (st.w_packed ? 0.5 : 1.0) * c.cout * c.cin * c.kh * c.kw + outb + resb;
     if (st.aux_src >= 0 && e->steps[st.aux_src].fused) {   // the downsample's GEMM runs here
         const ConvSpec& d = e->q[e->steps[st.aux_src].conv].spec;
         *macs += pos * d.cout * (double)d.cin;
@@ -2063,6 +2105,22 @@ int ptq8_engine_profile(ptq8_engine* e, int n, int iters, float* ms, double* mac
     cudaEventDestroy(a);
     cudaEventDestroy(b);
     return ptq8_engine_check_device_error(e);
+}
+
+int ptq8_engine_weight_bytes(const ptq8_engine* e, size_t* device_bytes, size_t* int8_bytes, int* packed_convs) {
+    if (!e || !e->planned) return PTQ8_ERR_INVALID;
+    size_t dev = 0, i8 = 0;
+    int np = 0;
+    for (const Step& st : e->steps) {
+        if (st.kind == K_MAXPOOL) continue;
+        dev += st.w_dev_bytes;
+        i8 += st.w_packed ? 2 * st.w_dev_bytes : st.w_dev_bytes;
+        np += st.w_packed ? 1 : 0;
+    }
+    if (device_bytes) *device_bytes = dev;
+    if (int8_bytes) *int8_bytes = i8;
+    if (packed_convs) *packed_convs = np;
+    return PTQ8_OK;
 }
 
 int ptq8_engine_n_launches(const ptq8_engine* e) {

@@ -716,7 +716,32 @@ struct ConvGeom {
     int* err;
     long long wait_limit;
     int stall_first_load;
+    // W4 weights stored two codes per byte (b_packed, resident slabs only): w4 = [w_rows][w4_ld]
+    // bytes, byte k/2 of row n holds code k in its low nibble and code k+1 in its high nibble
+    // (k even, K-major like the int8 matrix); the epilogue warps unpack the N tile's slab
+    // into the swizzled shared-memory layout of the TMA-loaded int8 weights
+    const uint8_t* w4;
+    int w4_ld, w_rows, b_packed;
 };
+
+// Sign-extended int8 codes of the 8 int4 codes in packed word x (low nibble first):
+// lo/hi = codes 8i+0..3 / 8i+4..7 as bytes.
+__device__ __forceinline__ void unpack_w4(uint32_t x, uint32_t& lo, uint32_t& hi) {
+    uint32_t a = x & 0x0F0F0F0Fu;          // codes 0, 2, 4, 6 (nibbles)
+    uint32_t b = (x >> 4) & 0x0F0F0F0Fu;   // codes 1, 3, 5, 7
+    a |= (a & 0x08080808u) * 0x1Eu;        // nibble bit 3 set -> byte 0xF0 | nibble (no carry between bytes)
+    b |= (b & 0x08080808u) * 0x1Eu;
+    lo = __byte_perm(a, b, 0x5140);        // a.b0 b.b0 a.b1 b.b1
+    hi = __byte_perm(a, b, 0x7362);        // a.b2 b.b2 a.b3 b.b3
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the tensor core
+// (async proxy) once the consumer has synchronised with it.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 constexpr int kEpiWarps = 16;                      // 4 per TMEM lane quadrant
 constexpr int kConvThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
@@ -777,7 +802,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
-        mbar_init(bfull, 1);
+        // resident weights: the producer's TMA loads (int8 slab, or the aux weights only when
+        // the slab is packed) and, for a packed slab, the epilogue warps' unpack
+        mbar_init(bfull, (g.b_packed ? 1u : 0u) + ((!g.b_packed || AUX) ? 1u : 0u));
         for (int b = 0; b < NA; ++b) {
             mbar_init(accf0 + 8 * b, 1);
             mbar_init(acce0 + 8 * b, group_warps);
@@ -807,11 +834,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         uint32_t last_ph = 0;   // bit s: parity of the last load issued into stage s
         uint32_t used = 0;      // bit s: stage s received at least one load
         bool ok = true;
-        if (g.b_resident) {
+        if (g.b_resident && (!g.b_packed || AUX)) {
             if (elect_one()) {
-                mbar_expect_tx(bfull, g.b_bytes * g.n_kchunks + (AUX ? static_cast<uint32_t>(BN * g.aux_kb) : 0u));
-                for (int kc = 0; kc < g.n_kchunks; ++kc)
-                    tma_load_2d(smem_u32(sB + kc * sb_stride), &map_b, bfull, kc * CB, nt * BN);
+                mbar_expect_tx(bfull, (g.b_packed ? 0u : g.b_bytes * g.n_kchunks) +
+                                          (AUX ? static_cast<uint32_t>(BN * g.aux_kb) : 0u));
+                if (!g.b_packed)
+                    for (int kc = 0; kc < g.n_kchunks; ++kc)
+                        tma_load_2d(smem_u32(sB + kc * sb_stride), &map_b, bfull, kc * CB, nt * BN);
                 if (AUX) tma_load_2d(smem_u32(sBx), &map_xb, bfull, 0, nt * BN);
             }
             __syncwarp();
@@ -942,6 +971,36 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         // Warps form NG groups; group gi takes tiles t = gi (mod NG), held in accumulator
         // t % NA, so NA tiles are in flight.  Inside a group the warps of a quadrant take
         // interleaved 16-column groups.
+        if (g.b_packed) {
+            // Packed W4 slab -> int8 codes in the swizzled layout TMA would have written:
+            // chunk kc holds rows n < BN of CB bytes, and the 16-byte granule of byte offset
+            // o = n*CB + 16j sits at o ^ (((o >> 7) & m) << 4) (m = 7 / 3 / 1 for the 128 /
+            // 64 / 32-byte swizzle; chunks are 1024-byte aligned).  Rows past the weight
+            // matrix are zero, as TMA's out-of-bounds fill.  The weights are constants:
+            // this runs before griddepcontrol.wait, under the previous kernel's tail.
+            constexpr uint32_t kSwz = CB == 128 ? 7u : (CB == 64 ? 3u : 1u);
+            constexpr int kGran = CB / 16;
+            const int per_chunk = BN * kGran;
+            const int total = g.n_kchunks * per_chunk;
+            for (int u = static_cast<int>(threadIdx.x) - 64; u < total; u += 32 * kEpiWarps) {
+                const int kc = u / per_chunk;
+                const int rem = u - kc * per_chunk;
+                const int n = rem / kGran, j = rem - (rem / kGran) * kGran;
+                const int row = nt * BN + n;
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (row < g.w_rows) {
+                    const uint2 p = __ldg(reinterpret_cast<const uint2*>(
+                        g.w4 + static_cast<size_t>(row) * g.w4_ld + kc * (CB / 2) + 8 * j));
+                    unpack_w4(p.x, v.x, v.y);
+                    unpack_w4(p.y, v.z, v.w);
+                }
+                const uint32_t o = static_cast<uint32_t>(n * CB + 16 * j);
+                *reinterpret_cast<uint4*>(sB + kc * sb_stride + (o ^ (((o >> 7) & kSwz) << 4))) = v;
+            }
+            fence_proxy_async_smem();
+            named_bar_sync(1, 32 * kEpiWarps);
+            if (threadIdx.x == 64) mbar_arrive(bfull);
+        }
         const int ew = warp - 2;
         const int gi = ew / group_warps;
         const int quad = warp & 3;
@@ -1363,6 +1422,7 @@ struct DwGeom {
     FastDiv fd_strips, fd_rs, fd_bands;   // strips, R * strips, bands
     int* err;              // the engine's device error word
     long long wait_limit;  // bounded-wait limit, clock cycles
+    int w_packed;          // W4 conv: the weight table holds 16-bit words of 3 int4 codes (see dw3x3_kernel)
 };
 
 constexpr int kDwMaxStages = 4;
@@ -1459,7 +1519,20 @@ __global__ void __launch_bounds__(kDwMaxConsumers + 32, 1) dw3x3_kernel(const in
     const uint32_t g = threadIdx.x % static_cast<uint32_t>(G4);
     const int c0 = 4 * static_cast<int>(g);
     uint32_t w[12];   // w[3 j + ... ]: column j, channel c at w[4 j + c]
-    {
+    if (d.w_packed) {
+        // W4: 12 16-bit words per group (24 bytes), word 4j + c = codes (w0j, w1j, w2j) of
+        // channel 4g + c as nibbles 0-2; spread to bytes and sign-extended
+        const uint2* p = reinterpret_cast<const uint2*>(wt) + 3 * g;
+        const uint2 a = __ldg(p), b = __ldg(p + 1), c = __ldg(p + 2);
+        const uint32_t hw[6] = {a.x, a.y, b.x, b.y, c.x, c.y};
+#pragma unroll
+        for (int t = 0; t < 12; ++t) {
+            const uint32_t h = (hw[t >> 1] >> (16 * (t & 1))) & 0xFFFu;
+            uint32_t x = (h & 0xFu) | ((h & 0xF0u) << 4) | ((h & 0xF00u) << 8);
+            x |= (x & 0x080808u) * 0x1Eu;
+            w[t] = x;
+        }
+    } else {
         const uint4 a = __ldg(wt + 3 * g), b = __ldg(wt + 3 * g + 1), c = __ldg(wt + 3 * g + 2);
         w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
         w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;

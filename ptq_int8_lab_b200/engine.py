@@ -44,7 +44,7 @@ EXPORTS = (
     "ptq8_engine_forward_device", "ptq8_engine_forward_async", "ptq8_engine_input_buffer", "ptq8_engine_logits_buffer", "ptq8_engine_run", "ptq8_engine_copy_logits",
     "ptq8_engine_sync", "ptq8_engine_check_device_error", "ptq8_engine_set_wait_test", "ptq8_engine_tensor_info",
     "ptq8_engine_dump", "ptq8_engine_dump_range",
-    "ptq8_engine_n_launches", "ptq8_engine_passes_log", "ptq8_engine_profile",
+    "ptq8_engine_n_launches", "ptq8_engine_weight_bytes", "ptq8_engine_passes_log", "ptq8_engine_profile",
     "ptq8_load", "ptq8_forward", "ptq8_forward_debug", "ptq8_capture_graph", "ptq8_destroy", "ptq8_last_error",
 )
 
@@ -115,6 +115,7 @@ def lib() -> ctypes.CDLL:
         "ptq8_engine_dump": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_size]),
         "ptq8_engine_dump_range": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size]),
         "ptq8_engine_n_launches": (c_int, [c_void_p]),
+        "ptq8_engine_weight_bytes": (c_int, [c_void_p, P(c_size), P(c_size), P(c_int)]),
         "ptq8_engine_profile": (c_int, [c_void_p, c_int, c_int, P(ctypes.c_float), P(ctypes.c_double),
                                         P(ctypes.c_double), P(c_int), c_int, P(c_int)]),
         "ptq8_engine_passes_log": (c_int, [c_void_p, c_char_p, c_size]),
@@ -332,6 +333,12 @@ class Int8Engine:
 
     def n_launches(self) -> int:
         return lib().ptq8_engine_n_launches(self._h)
+
+    def weight_bytes(self) -> dict:
+        """Conv weight bytes in device memory, the same weights as int8 bytes, packed W4 convs."""
+        dev, i8, npk = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_int()
+        self._check(lib().ptq8_engine_weight_bytes(self._h, ctypes.byref(dev), ctypes.byref(i8), ctypes.byref(npk)))
+        return {"device_bytes": dev.value, "int8_bytes": i8.value, "packed_w4_convs": npk.value}
 
     def profile(self, n: int, iters: int = 5) -> List[dict]:
         """Per-step device time (ms) and algorithmic work (see ptq8_engine_profile)."""

@@ -68,6 +68,37 @@ def test_batch_512_full_grid(make_model):
     compare(eng, tr, om, 512, logits)
 
 
+def test_w4_packed_config3(make_model):
+    """Config 3 (MobileNetV2 W4/W8 mixed): the W4 convs hold their codes two per byte in
+    device memory (unpacked into shared memory by the conv kernel, into registers by the
+    depthwise kernel) and stay bit-exact."""
+    paths = make_model(3)
+    eng, tr, om, logits = _run(paths, 6, seed=19)
+    compare(eng, tr, om, 6, logits)
+    wb = eng.weight_bytes()
+    assert wb["packed_w4_convs"] > 0, wb
+    assert wb["device_bytes"] < wb["int8_bytes"], wb
+
+
+def test_w4_resnet18_all_layers(make_model):
+    """ResNet-18 at W4 on every conv (the reference's W4A8 run, ROOFLINE-int8.md:609-626):
+    layers 1-2 keep resident weight slabs (packed; 64- and 128-byte swizzles), layers 3-4
+    stream theirs (int8 storage)."""
+    from ptq_int8_lab_b200 import engine as E
+    paths = make_model("resnet18", seed=0, bn="data")
+    m = E.Model.load(paths["model"])
+    eng = E.Int8Engine(0)
+    eng.build(m, 4, 8)
+    eng.set_calib(E.load_ptqc(paths["calib"], m.n_conv))
+    eng.alloc_scratch(8)
+    x = np.random.default_rng(23).standard_normal((7, 3, 32, 32)).astype(np.float32)
+    logits = eng.forward(x)
+    om = O.read_model(paths["model"])
+    tr = O.Oracle(om, O.read_ptqc(paths["calib"]), layer_bits=[4] * m.n_conv).forward(x)
+    compare(eng, tr, om, 7, logits)
+    assert eng.weight_bytes()["packed_w4_convs"] >= 8
+
+
 RAGGED_MV2 = ((1, 16, 1, 1), (3, 40, 1, 2), (1, 40, 1, 1), (3, 24, 1, 2))
 
 

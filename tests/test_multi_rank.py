@@ -27,8 +27,15 @@ def _worker(rank: int, world: int, port: int, cache: str, out: str):
     import bench
     r, w, local = bench.dist_env()
     paths = bench.model_files(cache, r, w, dist.barrier, cfg=0)
+    import torch
+    B = 5
+    local_logits = torch.arange(B * 10, dtype=torch.float32).reshape(B, 10) + 1000.0 * r
+    gathered = torch.empty(w * B, 10, dtype=torch.float32)
+    bench.gather_logits(gathered, local_logits)
     res = {"env": [r, w, local], "paths": paths, "sizes": {k: os.path.getsize(v) for k, v in paths.items()},
-           "max_ms": bench.max_over_ranks(10.0 * (r + 1), "cpu")}
+           "max_ms": bench.max_over_ranks(10.0 * (r + 1), "cpu"),
+           "all_ms": bench.all_ranks(1.5 + r, "cpu"),
+           "gathered": gathered.tolist()}
     dist.barrier()
     dist.destroy_process_group()
     with open(os.path.join(out, f"rank{rank}.json"), "w") as f:
@@ -43,6 +50,12 @@ def test_two_ranks_share_model_files_and_max_time(tmp_path):
     assert r[0]["paths"] == r[1]["paths"]
     assert all(v > 0 for v in r[0]["sizes"].values()) and r[0]["sizes"] == r[1]["sizes"]
     assert r[0]["max_ms"] == r[1]["max_ms"] == 20.0
+    assert r[0]["all_ms"] == r[1]["all_ms"] == [1.5, 2.5]
+    # every rank holds every rank's logits, in rank order
+    import numpy as np
+    want = np.concatenate([np.arange(50, dtype=np.float32).reshape(5, 10) + 1000.0 * k for k in range(world)])
+    for x in r:
+        assert np.array_equal(np.asarray(x["gathered"], dtype=np.float32), want)
 
 
 def test_single_process_max_is_identity():
