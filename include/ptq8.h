@@ -45,22 +45,31 @@ int ptq8_abi_version(void);
 /* ---- calibrated-model files ------------------------------------------------ */
 
 /* Model::load(path, err) - 06-gpu-int8/cpp/ptq_model.h:72-91.
- * PTQW or PTQ2 by magic, strict EOF, topology validation (ptq_model.h:104-203).
- * Returns NULL on failure with the reason in err. */
+ * PTQW or PTQ2 by magic, strict EOF, topology validation (ptq_model.h:104-203);
+ * also PTQ8, this engine's native package (weight codes, f32 scales and bits per conv,
+ * W4 two codes per byte; layout in csrc/ptq8_model.hpp), which builds without
+ * re-quantizing.  Returns NULL on failure with the reason in err. */
 ptq8_model* ptq8_model_load(const char* path, char* err, size_t errlen);
 void ptq8_model_free(ptq8_model* m);
 
 /* Counters of Model (ptq_model.h:65-70,205-229): out[11] = {n_conv, n_block,
  * stem_pool, fc_in, fc_out, n_depthwise, n_grouped, n_relu6, n_residual2,
- * format (1 PTQW, 2 PTQ2), convs per block}. */
+ * format (1 PTQW, 2 PTQ2, 3 PTQ8), convs per block}. */
 int ptq8_model_info(const ptq8_model* m, int* out);
 /* ConvSpec of conv i (ptq_model.h:46-55): {cout, cin, kh, kw, sh, sw, ph, pw, relu, groups}. */
 int ptq8_model_conv(const ptq8_model* m, int i, int* meta10);
 /* BlockSpec of block i (ptq_model.h:57-63). */
 int ptq8_model_block(const ptq8_model* m, int i, int* convs, int cap, int* n_convs, int* ds, int* stride,
                      int* residual);
-/* Borrowed pointers to conv i's fp32 weight/bias (i = -1: the FC). */
+/* Borrowed pointers to conv i's fp32 weight/bias (i = -1: the FC).  A PTQ8 conv has no
+ * fp32 weights (n_weight 0). */
 int ptq8_model_weights(const ptq8_model* m, int i, const float** weight, size_t* n_weight, const float** bias);
+/* Borrowed pointers to conv i's stored codes ([cout][cin*kh*kw], one per byte) and f32
+ * per-channel scales, and its bits (8 / 4), from a PTQ8 package; bits 0 and NULL
+ * pointers for a PTQ2 / PTQW conv.  No counterpart in the reference (its files hold fp32
+ * weights that Int8Engine::build quantizes, int8_engine.cuh:208). */
+int ptq8_model_codes(const ptq8_model* m, int i, const int8_t** codes, size_t* n_codes, const float** scales,
+                     int* bits);
 
 /* load_ptqc(path, n_expected, out, err) - 06-gpu-int8/cpp/ptq_model.h:425-503.
  * Writes n (lo, hi) pairs to lohi[2n] (cap = number of floats available). */

@@ -1505,7 +1505,7 @@ int ptq8_model_info(const ptq8_model* mm, int* out) {
     out[6] = n_grouped;
     out[7] = n_relu6;
     out[8] = n_res2;
-    out[9] = m.magic == "PTQ2" ? 2 : 1;
+    out[9] = m.magic == "PTQ8" ? 3 : (m.magic == "PTQ2" ? 2 : 1);
     out[10] = m.blocks.empty() ? 0 : (int)m.blocks[0].convs.size();
     return PTQ8_OK;
 }
@@ -1542,6 +1542,17 @@ int ptq8_model_weights(const ptq8_model* mm, int i, const float** weight, size_t
     if (weight) *weight = c.weight.data();
     if (n_weight) *n_weight = c.weight.size();
     if (bias) *bias = c.bias.data();
+    return PTQ8_OK;
+}
+
+int ptq8_model_codes(const ptq8_model* mm, int i, const int8_t** codes, size_t* n_codes, const float** scales,
+                     int* bits) {
+    if (!mm || i < 0 || i >= (int)mm->m.convs.size()) return PTQ8_ERR_INVALID;
+    const ConvSpec& c = mm->m.convs[i];
+    if (codes) *codes = c.codes.empty() ? nullptr : c.codes.data();
+    if (n_codes) *n_codes = c.codes.size();
+    if (scales) *scales = c.wscale.empty() ? nullptr : c.wscale.data();
+    if (bits) *bits = c.qbits;
     return PTQ8_OK;
 }
 
@@ -1700,6 +1711,14 @@ int ptq8_engine_build(ptq8_engine* e, const ptq8_model* mm, int w_bits, int a_bi
                     return e->fail(strf("layer plan: conv %zu bits=%d (4/8 only)", i, layer_bits[i]));
                 e->layer_bits[i] = layer_bits[i];
             }
+        // a PTQ8 package carries each conv's codes and bits: they rule (a plan must agree)
+        for (size_t i = 0; i < m.convs.size(); ++i) {
+            const int qb = m.convs[i].qbits;
+            if (qb == 0) continue;
+            if (layer_bits && layer_bits[i] != qb)
+                return e->fail(strf("layer plan: conv %zu bits=%d but the package stores W%d codes", i, layer_bits[i], qb));
+            e->layer_bits[i] = qb;
+        }
         std::string verr;
         if (!m.validate(&verr, e->in_h, e->in_w)) return e->fail(verr);
         e->q.assign(m.convs.size(), ConvQ());
@@ -1709,11 +1728,18 @@ int ptq8_engine_build(ptq8_engine* e, const ptq8_model* mm, int w_bits, int a_bi
             cq.spec = c;
             cq.spec.weight.clear();
             cq.spec.bias.clear();
+            cq.spec.codes.clear();
+            cq.spec.wscale.clear();
             cq.bits = e->layer_bits[i];
             const int K = c.cin * c.kh * c.kw;
-            cq.codes.resize((size_t)c.cout * K);
-            cq.wscale.resize(c.cout);
-            quantize_weight_per_channel(c.weight.data(), c.cout, K, cq.bits, cq.codes.data(), cq.wscale.data());
+            if (c.qbits > 0) {   // PTQ8: the stored codes and scales, no re-quantization
+                cq.codes = c.codes;
+                cq.wscale = c.wscale;
+            } else {
+                cq.codes.resize((size_t)c.cout * K);
+                cq.wscale.resize(c.cout);
+                quantize_weight_per_channel(c.weight.data(), c.cout, K, cq.bits, cq.codes.data(), cq.wscale.data());
+            }
             cq.bias = c.bias;
         }
         // graph passes run on the quantized layers (codes + scales), so they are exact

@@ -164,8 +164,55 @@ bool load_ptqw(Reader& r, Model& m, std::string* err) {
     return read_fc(r, m, err);
 }
 
-bool load_ptq2(Reader& r, Model& m, std::string* err) {
-    if (r.size() < 20) return fail(err, "file too short: less than magic + header (< 20 B)");
+// PTQ8 conv payload after the 10 meta ints: bits, f32 scales, f32 bias, codes (one byte
+// each for W8, two per byte for W4), unpacked here to one code per byte.
+bool read_native_payload(Reader& r, ConvSpec& c, int i, std::string* err) {
+    char what[64];
+    std::snprintf(what, sizeof what, "conv[%d].bits", i);
+    if (!r.i32(&c.qbits, what, err)) return false;
+    if (c.qbits != 8 && c.qbits != 4) return fail(err, fmt("conv[%d]: bits=%d (PTQ8 holds 8 or 4)", i, c.qbits));
+    std::snprintf(what, sizeof what, "conv[%d].w_scale", i);
+    if (!r.floats((size_t)c.cout, &c.wscale, what, err)) return false;
+    for (int o = 0; o < c.cout; ++o)
+        if (!std::isfinite(c.wscale[o]) || !(c.wscale[o] > 0.0f))
+            return fail(err, fmt("conv[%d]: w_scale[%d] is not finite and positive", i, o));
+    std::snprintf(what, sizeof what, "conv[%d].bias", i);
+    if (!r.floats((size_t)c.cout, &c.bias, what, err)) return false;
+    size_t k = 0, n = 0;
+    if (!mul_ok((size_t)c.cin, (size_t)c.kh, &k) || !mul_ok(k, (size_t)c.kw, &k) || !mul_ok(k, (size_t)c.cout, &n))
+        return fail(err, fmt("conv[%d]: code count overflows", i));
+    const size_t row = c.qbits == 8 ? k : (k + 1) / 2;
+    std::vector<uint8_t> raw;
+    size_t nb = 0;
+    if (!mul_ok(row, (size_t)c.cout, &nb)) return fail(err, fmt("conv[%d]: code bytes overflow", i));
+    if (nb > r.left())
+        return fail(err, fmt("conv[%d].codes: needs %zu B but only %zu B left - truncated", i, nb, r.left()));
+    raw.resize(nb);
+    std::snprintf(what, sizeof what, "conv[%d].codes", i);
+    if (!r.raw(raw.data(), nb, what, err)) return false;
+    c.codes.resize(n);
+    for (int o = 0; o < c.cout; ++o)
+        for (size_t j = 0; j < k; ++j) {
+            int8_t v;
+            if (c.qbits == 8) {
+                v = (int8_t)raw[(size_t)o * row + j];
+            } else {
+                const int nib = (raw[(size_t)o * row + j / 2] >> (4 * (j & 1))) & 0xF;
+                v = (int8_t)(nib >= 8 ? nib - 16 : nib);
+            }
+            c.codes[(size_t)o * k + j] = v;
+        }
+    return true;
+}
+
+// PTQ2 (and, with native = true, the PTQ8 package that shares its header, blocks and fc).
+bool load_ptq2(Reader& r, Model& m, std::string* err, bool native = false) {
+    if (r.size() < (native ? 24u : 20u)) return fail(err, "file too short: less than magic + header");
+    if (native) {
+        int version = 0;
+        if (!r.i32(&version, "header.version", err)) return false;
+        if (version != 1) return fail(err, fmt("PTQ8 version %d unsupported (1 only)", version));
+    }
     int n_conv = 0, n_block = 0, ncp = 0;
     if (!r.i32(&n_conv, "header.n_conv", err) || !r.i32(&n_block, "header.n_block", err) ||
         !r.i32(&m.stem_pool, "header.stem_pool", err) || !r.i32(&ncp, "header.n_conv_per_block", err))
@@ -187,7 +234,8 @@ bool load_ptq2(Reader& r, Model& m, std::string* err) {
             std::snprintf(what, sizeof what, "conv[%d].meta[%d]", i, k);
             if (!r.i32(meta[k], what, err)) return false;
         }
-        if (!conv_meta_ok(c, i, err) || !read_conv_payload(r, c, i, err)) return false;
+        if (!conv_meta_ok(c, i, err)) return false;
+        if (!(native ? read_native_payload(r, c, i, err) : read_conv_payload(r, c, i, err))) return false;
     }
     m.blocks.resize((size_t)n_block);
     for (int i = 0; i < n_block; i++) {
@@ -232,6 +280,9 @@ bool Model::load(const std::string& path, std::string* err) {
     } else if (std::memcmp(mg, "PTQ2", 4) == 0) {
         m.magic = "PTQ2";
         ok = load_ptq2(r, m, err);
+    } else if (std::memcmp(mg, "PTQ8", 4) == 0) {
+        m.magic = "PTQ8";
+        ok = load_ptq2(r, m, err, true);
     } else {
         std::string p;
         for (int i = 0; i < 4; i++) {
@@ -239,7 +290,7 @@ bool Model::load(const std::string& path, std::string* err) {
             if (ch >= 32 && ch < 127) p.push_back((char)ch);
             else p += fmt("\\x%02x", ch);
         }
-        return fail(err, path + ": bad magic (expected PTQW/PTQ2, got '" + p + "')");
+        return fail(err, path + ": bad magic (expected PTQW/PTQ2/PTQ8, got '" + p + "')");
     }
     if (!ok) return false;
     if (r.pos() != r.size())

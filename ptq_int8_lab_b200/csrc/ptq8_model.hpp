@@ -14,6 +14,14 @@
 //         per block (ncp + 3) x i32 (convs..., -1 padded, ds, stride, residual); fc.
 //   PTQC  09-ptq-toolkit/ptq_toolkit/export/ptqc.py:1-20, read by ptq_model.h:425-503
 //         "PTQC", i32 n, n x (f32 lo, f32 hi); size exactly 8 + 8n.
+//   PTQ8  this engine's native package (no reference counterpart: the reference's PTQ2
+//         stores every layer, W4 included, as fp32 QDQ values, pipeline.py:272-279):
+//         "PTQ8", i32 version (1), n_conv, n_block, stem_pool, ncp;
+//         per conv 10 x i32 as PTQ2, i32 bits (8 or 4), f32 w_scale[cout], f32 bias[cout],
+//         codes: bits 8 -> int8 [cout][K]; bits 4 -> [cout][ceil(K/2)] bytes, code k of a
+//         row in the low nibble of byte k/2 for even k, the high nibble for odd k
+//         (K = cin * kh * kw in (c, i, j) order, the per-channel codes of
+//         ptq_quant.h:72-110); per block (ncp + 3) x i32 as PTQ2; fc as PTQ2.
 //
 // Error behaviour mirrors the reference loaders: every failure returns false
 // with a message, nothing exits, truncated files and trailing bytes are
@@ -32,8 +40,12 @@ struct ConvSpec {
     int sh = 1, sw = 1, ph = 0, pw = 0;
     int relu = 0;                             // 0 none, 1 ReLU, 2 ReLU6
     int groups = 1;
-    std::vector<float> weight;                // [cout][cin][kh][kw]
+    std::vector<float> weight;                // [cout][cin][kh][kw] (empty when qbits > 0)
     std::vector<float> bias;                  // [cout]
+    // PTQ8: the per-channel codes and f32 scales as stored (qbits 8 or 4; 0 for fp32 weights)
+    int qbits = 0;
+    std::vector<int8_t> codes;                // [cout][cin * kh * kw], one code per byte
+    std::vector<float> wscale;                // [cout]
     int in_channels() const { return cin * groups; }
     bool depthwise() const { return cin == 1 && groups == cout && groups > 1; }
 };
@@ -51,7 +63,7 @@ struct Model {
     int stem_pool = 0;
     int fc_in = 0, fc_out = 0;
     std::vector<float> fc_w, fc_b;   // [fc_out][fc_in], [fc_out]
-    std::string magic;               // "PTQW" or "PTQ2"
+    std::string magic;               // "PTQW", "PTQ2" or "PTQ8"
 
     // Model::load (ptq_model.h:72-91): dispatch on magic, strict parse, validate.
     bool load(const std::string& path, std::string* err);

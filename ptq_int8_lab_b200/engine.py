@@ -36,7 +36,7 @@ ACT_MINMAX = 1
 # every symbol include/ptq8.h declares
 EXPORTS = (
     "ptq8_abi_version", "ptq8_model_load", "ptq8_model_free", "ptq8_model_info", "ptq8_model_conv",
-    "ptq8_model_block", "ptq8_model_weights", "ptq8_load_ptqc", "ptq8_act_scale", "ptq8_quantize_weight", "ptq8_quantize_device",
+    "ptq8_model_block", "ptq8_model_weights", "ptq8_model_codes", "ptq8_load_ptqc", "ptq8_act_scale", "ptq8_quantize_weight", "ptq8_quantize_device",
     "ptq8_quantize_device_noalloc",
     "ptq8_engine_create", "ptq8_engine_destroy", "ptq8_engine_last_error", "ptq8_engine_build",
     "ptq8_engine_set_act_mode", "ptq8_engine_set_calib", "ptq8_engine_set_input_shape",
@@ -83,6 +83,8 @@ def lib() -> ctypes.CDLL:
         "ptq8_model_conv": (c_int, [c_void_p, c_int, P(c_int)]),
         "ptq8_model_block": (c_int, [c_void_p, c_int, P(c_int), c_int, P(c_int), P(c_int), P(c_int), P(c_int)]),
         "ptq8_model_weights": (c_int, [c_void_p, c_int, P(P(ctypes.c_float)), P(c_size), P(P(ctypes.c_float))]),
+        "ptq8_model_codes": (c_int, [c_void_p, c_int, P(P(ctypes.c_int8)), P(c_size), P(P(ctypes.c_float)),
+                                     P(c_int)]),
         "ptq8_load_ptqc": (c_int, [c_char_p, c_size, P(ctypes.c_float), c_size, c_char_p, c_size]),
         "ptq8_act_scale": (ctypes.c_double, [ctypes.c_float, ctypes.c_float, c_int, c_int]),
         "ptq8_quantize_weight": (c_int, [P(ctypes.c_float), c_int, c_int, c_int, P(ctypes.c_int8), P(ctypes.c_float)]),
@@ -150,7 +152,7 @@ class Model:
         lib().ptq8_model_info(handle, info)
         (self.n_conv, self.n_block, self.stem_pool, self.fc_in, self.fc_out, self.n_depthwise,
          self.n_grouped, self.n_relu6, self.n_residual2, fmt, self.n_conv_per_block) = list(info)
-        self.format = "PTQ2" if fmt == 2 else "PTQW"
+        self.format = {1: "PTQW", 2: "PTQ2", 3: "PTQ8"}[fmt]
 
     @classmethod
     def load(cls, path) -> "Model":
@@ -183,7 +185,21 @@ class Model:
         if lib().ptq8_model_weights(self._h, i, ctypes.byref(w), ctypes.byref(n), ctypes.byref(b)):
             raise IndexError(i)
         nb = self.fc_out if i == -1 else self.conv(i)["cout"]
-        return (np.ctypeslib.as_array(w, shape=(n.value,)).copy(), np.ctypeslib.as_array(b, shape=(nb,)).copy())
+        wa = np.ctypeslib.as_array(w, shape=(n.value,)).copy() if n.value else np.zeros(0, np.float32)  # PTQ8: none
+        return wa, np.ctypeslib.as_array(b, shape=(nb,)).copy()
+
+    def codes(self, i: int):
+        """(codes [cout, K] int8, f32 scales [cout], bits) stored by a PTQ8 package; None for PTQ2/PTQW."""
+        c = ctypes.POINTER(ctypes.c_int8)()
+        s = ctypes.POINTER(ctypes.c_float)()
+        n, b = ctypes.c_size_t(), ctypes.c_int()
+        if lib().ptq8_model_codes(self._h, i, ctypes.byref(c), ctypes.byref(n), ctypes.byref(s), ctypes.byref(b)):
+            raise IndexError(i)
+        if b.value == 0:
+            return None
+        cout = self.conv(i)["cout"]
+        return (np.ctypeslib.as_array(c, shape=(n.value,)).reshape(cout, -1).copy(),
+                np.ctypeslib.as_array(s, shape=(cout,)).copy(), b.value)
 
     def __del__(self):
         h, self._h = getattr(self, "_h", None), None
