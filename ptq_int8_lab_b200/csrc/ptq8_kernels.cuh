@@ -88,12 +88,16 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete: false after
-// `limit` clock cycles without completion.
+// `limit` clock cycles without completion.  The clock is read once per 8 tries
+// (a try per clock read made the polling warps issue several times more
+// instructions than the tries themselves).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long limit) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
-        if (mbar_try(bar, parity)) return true;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (mbar_try(bar, parity)) return true;
         if (clock64() - t0 > limit) return false;
     }
 }
@@ -747,6 +751,157 @@ constexpr int kEpiWarps = 16;                      // 4 per TMEM lane quadrant
 constexpr int kConvThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int kMaxStages = 24;
 
+// Epilogue of a halo-block conv (mode 1) whose single N tile is the whole output:
+// cout == FBN (64 or 128, a compile-time constant), no positional decomposition.
+// Every channel offset is then a compile-time constant: the (factor, bias) pairs
+// are constant-bank operands of the multiply and the add (no loads), the fp32
+// row and code-row offsets of a 16-channel half are immediates, and the column
+// loop is unrolled.  A thread's row walks the tiles of its group by a fixed step
+// of bordered positions, so (image, row, column) advance by carries instead of
+// divisions.  Warps: NG groups (4, or 2 when two accumulators fit) of 16 / NG
+// warps; group gi drains accumulators gi, gi + NG, ...; with NG = 2 the two warps
+// of a lane quadrant split the columns in halves.  Numerics are those of the
+// general epilogue below (same dequant16 / quant16q calls in the same order).
+template <int CB, int NOUT, bool RES, bool F32, bool AUX, int FBN>
+__device__ __forceinline__ void epilogue_fast(const ConvGeom& g, const EpiParams& e, const ConvConsts& cc,
+                                              uint32_t tmem, uint32_t accf0, uint32_t acce0, int warp, int lane) {
+    static_assert(FBN == 64 || FBN == 128, "fast epilogue: 64 or 128 output channels");
+    constexpr int HALVES = FBN / 16;
+    const int NG = g.n_groups;
+    const int NA = g.n_acc;
+    const int gw = kEpiWarps / NG;
+    const int ew = warp - 2;
+    const int gi = ew / gw;
+    const int quad = warp & 3;
+    const int slice = (ew % gw) >> 2;
+    const int r = quad * 32 + lane;
+    const int h_lo = NG == 4 ? 0 : slice * (HALVES / 2);
+    const int h_hi = NG == 4 ? HALVES : h_lo + HALVES / 2;
+    // quantizer clamps with the activation / post-add ReLU folded where no fp32 value is kept
+    constexpr bool kFold = !RES && !F32 && !AUX;
+    constexpr bool kFoldPost = RES && !F32;
+    const bool nonneg = RES ? e.post == 1 : e.act != 0;
+    QParams qx[2] = {e.q0, e.q1};
+    if (kFold) {
+        qx[0] = fold_act(e.q0, e.act);
+        qx[1] = fold_act(e.q1, e.act);
+    } else if (nonneg) {
+        qx[0].y_lo = 0.0f;
+        qx[1].y_lo = 0.0f;
+    }
+    const double sq[2] = {e.s0, e.s1};
+    const int act = kFold ? 0 : e.act;
+    const bool check = !e.acc_small;
+    griddep_wait();   // residuals are earlier kernels' outputs
+
+    const uint32_t img = g.fd_img.d, Wp = g.fd_wp.d, Hp = static_cast<uint32_t>(g.Hp);
+    const uint32_t step = static_cast<uint32_t>(NG) * gridDim.x * 128u;
+    uint32_t q = (blockIdx.x + static_cast<uint32_t>(gi) * gridDim.x) * 128u + static_cast<uint32_t>(r);
+    uint32_t n = fdiv(q, g.fd_img);
+    uint32_t hb = fdiv(q - n * img, g.fd_wp);
+    uint32_t wb = q - n * img - hb * Wp;
+    const uint32_t sn = fdiv(step, g.fd_img);
+    const uint32_t sh = fdiv(step - sn * img, g.fd_wp);
+    const uint32_t sw = step - sn * img - sh * Wp;
+
+    int buf = gi;
+    uint32_t use = 0;
+    for (int mt = blockIdx.x + gi * gridDim.x; mt < g.m_tiles; mt += NG * gridDim.x) {
+        const int h = static_cast<int>(hb) - 1, w = static_cast<int>(wb) - 1;
+        const bool valid = n < static_cast<uint32_t>(g.N) && h >= 0 && h < g.OH && w >= 0 && w < g.OW;
+        const bool even = ((h | w) & 1) == 0;
+        // fp32 map offset of channel 0 of this position (tiled layout, C = FBN)
+        const uint32_t pf = (n * static_cast<uint32_t>(g.OH) + static_cast<uint32_t>(h)) * static_cast<uint32_t>(g.OW) +
+                            static_cast<uint32_t>(w);
+        const size_t fo = static_cast<size_t>(pf >> 5) * (FBN * 32) + (pf & 31u) * 8u;
+        int8_t* qrow[2] = {nullptr, nullptr};
+        bool kept[2] = {false, false};
+#pragma unroll
+        for (int o = 0; o < NOUT; ++o) {
+            const bool sub = (e.sub_mask >> o) & 1;
+            kept[o] = valid && (!sub || even);
+            const size_t pq = sub ? (static_cast<size_t>(n) * (e.sub_h + 2) + (h >> 1) + 1) * (e.sub_w + 2) + (w >> 1) + 1
+                                  : static_cast<size_t>(q);
+            qrow[o] = (o == 0 ? e.out_q0 : e.out_q1) + pq * static_cast<size_t>(o == 0 ? e.ldq0 : e.ldq1);
+        }
+        // the residual does not depend on the MMAs: fetch the first half before waiting
+        float res[16];
+        if (RES && !AUX && valid) {
+            ld_v8(e.residual + fo + static_cast<size_t>(2 * h_lo) * 256, &res[0]);
+            ld_v8(e.residual + fo + static_cast<size_t>(2 * h_lo + 1) * 256, &res[8]);
+        }
+        if (!mbar_wait(accf0 + 8 * buf, use & 1u, g.wait_limit)) {
+            atomicExch(g.err, ERR_WAIT_ACC);
+            break;
+        }
+        tc_fence_after();
+        const uint32_t trow = tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16);
+        uint32_t wq[2][8];
+#pragma unroll
+        for (int hh = 0; hh < HALVES; ++hh) {
+            if (hh < h_lo || hh >= h_hi) continue;
+            uint32_t v[16], vx[16];
+            __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the per-lane stores
+            tmem_ld16(trow + hh * 16, v);
+            if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + hh * 16, vx);
+            tmem_wait_ld();
+            if (!valid) continue;
+            float y[16];
+            dequant16(v, cc.fb + hh * 16, act, y, check);
+            if (AUX) dequant16(vx, cc.aux_fb + hh * 16, e.aux_act, res, false);   // aux K <= 128
+            if constexpr (RES) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                    const float2 t = add2_rn(make_float2(y[j], y[j + 1]), make_float2(res[j], res[j + 1]));
+                    y[j] = t.x;
+                    y[j + 1] = t.y;
+                }
+                if (!kFoldPost && e.post == 1) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.0f);
+                }
+            }
+            if constexpr (F32) {
+                st_v8(e.out_f32 + fo + static_cast<size_t>(2 * hh) * 256, &y[0]);
+                st_v8(e.out_f32 + fo + static_cast<size_t>(2 * hh + 1) * 256, &y[8]);
+            }
+            if (RES && !AUX && hh + 1 < h_hi) {   // next half's residual
+                ld_v8(e.residual + fo + static_cast<size_t>(2 * hh + 2) * 256, &res[0]);
+                ld_v8(e.residual + fo + static_cast<size_t>(2 * hh + 3) * 256, &res[8]);
+            }
+#pragma unroll
+            for (int o = 0; o < NOUT; ++o) {
+                if (!kept[o]) continue;
+                uint32_t w4[4];
+                quant16q<true>(y, qx[o], sq[o], w4);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) wq[o][(hh & 1) * 4 + j] = w4[j];
+                if (hh & 1) st_v8(reinterpret_cast<uint32_t*>(qrow[o] + (hh >> 1) * 32), wq[o]);
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_relaxed(acce0 + 8 * buf);
+        if ((buf += NG) >= NA) {
+            buf -= NA;
+            use ^= 1u;
+        }
+        // next tile of this group: step bordered positions further
+        wb += sw;
+        if (wb >= Wp) {
+            wb -= Wp;
+            ++hb;
+        }
+        hb += sh;
+        if (hb >= Hp) {
+            hb -= Hp;
+            ++n;
+        }
+        n += sn;
+        q += step;
+    }
+}
+
 // Persistent implicit-GEMM conv.  grid = (CTAs per N tile, N tiles); each CTA
 // walks M tiles blockIdx.x, blockIdx.x + gridDim.x, ...  Two TMEM accumulators
 // let the epilogue of tile i overlap the MMAs of tile i+1.
@@ -760,8 +915,9 @@ constexpr int kMaxStages = 24;
 // Template parameters fix the per-launch shape of the work so each launch runs
 // a lean instruction stream: CB = K-chunk bytes (swizzle width), MODE (above),
 // NOUT = int8 code outputs (0..2), RES = residual add, F32 = fp32 output,
-// AUX = the residual is the aux GEMM's output (map_xa / map_xb) instead of a load.
-template <int CB, int MODE, int NOUT, bool RES, bool F32, bool AUX>
+// AUX = the residual is the aux GEMM's output (map_xa / map_xb) instead of a load,
+// FBN = 64 / 128: mode 1 with that whole-output N tile, drained by epilogue_fast.
+template <int CB, int MODE, int NOUT, bool RES, bool F32, bool AUX, int FBN = 0>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const __grid_constant__ CUtensorMap map_xa, const __grid_constant__ CUtensorMap map_xb,
@@ -932,8 +1088,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
                 tc_fence_after();
                 const uint64_t da0 = adesc0 + static_cast<uint64_t>(s) * a_stage_step;
-                if (MODE == 1) {
-                    // 3x3 taps (mode 1 is planned only for 3x3 convs), fully unrolled
+                if (MODE == 1 && g.KH == 1) {
+                    // one tap (the stem GEMM over its bordered im2col rows): the block is the tile
+                    mma_chunk_elect<CB / 32>(d, da0, bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step, idesc,
+                                             ka != 0 ? 1u : 0u);
+                } else if (MODE == 1) {
+                    // 3x3 taps (mode 1 is planned only for 3x3 convs and the 1x1 stem GEMM), fully unrolled
                     uint64_t da_row = da0;
                     uint64_t db = bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step;
                     uint32_t acc = ka != 0 ? 1u : 0u;
@@ -1001,6 +1161,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             named_bar_sync(1, 32 * kEpiWarps);
             if (threadIdx.x == 64) mbar_arrive(bfull);
         }
+        if constexpr (FBN > 0) {
+            epilogue_fast<CB, NOUT, RES, F32, AUX, FBN>(g, e, cc, tmem, accf0, acce0, warp, lane);
+        } else {
         const int ew = warp - 2;
         const int gi = ew / group_warps;
         const int quad = warp & 3;
@@ -1223,6 +1386,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
         }
         }
+        }   // general epilogue
     }
     tc_fence_before();
     __syncthreads();
