@@ -223,6 +223,251 @@ __device__ __forceinline__ void mma_chunk_elect(uint32_t d, uint64_t da, uint64_
     }
 }
 
+// All MMAs of one 3x3 halo-block K chunk in one asm block with one election: A
+// descriptors of kernel row i start at a0 + i*arow (16-byte units; tap column j and
+// K slice k add the immediate j*CB/16 + 2k), B descriptors of tap t at b0 + t*btap
+// (+ 2k).  Only the low descriptor word carries the start address (14 bits, never
+// carrying into the high word inside shared memory), so each MMA costs two 32-bit
+// adds and the tensor-core instruction: issued this way the MMAs run at the tensor
+// core's rate (48 cycles per N = 64 MMA, 64 per N = 128), where one asm block per tap
+// with 64-bit descriptor arithmetic left the issuing warp at about 70-90 cycles per MMA.
+template <int KS>
+__device__ __forceinline__ void mma_3x3_chunk(uint32_t d, uint64_t da, uint64_t db, uint32_t arow, uint32_t btap,
+                                              uint32_t idesc, uint32_t acc);
+template <>
+__device__ __forceinline__ void mma_3x3_chunk<1>(uint32_t d, uint64_t da, uint64_t db, uint32_t arow, uint32_t btap,
+                                                 uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t.reg .b32 alo, ahi, blo, bhi, a1, a2, b1, b2, b3, b4, b5, b6, b7, b8, ta, tb;\n\t.reg .b64 A, B;\n\t"
+        "mov.b64 {alo, ahi}, %1;\n\tmov.b64 {blo, bhi}, %2;\n\t"
+        "add.u32 a1, alo, %5;\n\tadd.u32 a2, a1, %5;\n\t"
+        "add.u32 b1, blo, %6;\n\tadd.u32 b2, b1, %6;\n\tadd.u32 b3, b2, %6;\n\tadd.u32 b4, b3, %6;\n\t"
+        "add.u32 b5, b4, %6;\n\tadd.u32 b6, b5, %6;\n\tadd.u32 b7, b6, %6;\n\tadd.u32 b8, b7, %6;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "add.u32 ta, alo, 0;\n\tadd.u32 tb, blo, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, p;\n\t"
+        "add.u32 ta, alo, 2;\n\tadd.u32 tb, b1, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 4;\n\tadd.u32 tb, b2, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 0;\n\tadd.u32 tb, b3, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 2;\n\tadd.u32 tb, b4, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 4;\n\tadd.u32 tb, b5, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 0;\n\tadd.u32 tb, b6, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 2;\n\tadd.u32 tb, b7, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 4;\n\tadd.u32 tb, b8, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "}\n"
+        ::"r"(d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(arow), "r"(btap)
+        : "memory");
+}
+
+template <>
+__device__ __forceinline__ void mma_3x3_chunk<2>(uint32_t d, uint64_t da, uint64_t db, uint32_t arow, uint32_t btap,
+                                                 uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t.reg .b32 alo, ahi, blo, bhi, a1, a2, b1, b2, b3, b4, b5, b6, b7, b8, ta, tb;\n\t.reg .b64 A, B;\n\t"
+        "mov.b64 {alo, ahi}, %1;\n\tmov.b64 {blo, bhi}, %2;\n\t"
+        "add.u32 a1, alo, %5;\n\tadd.u32 a2, a1, %5;\n\t"
+        "add.u32 b1, blo, %6;\n\tadd.u32 b2, b1, %6;\n\tadd.u32 b3, b2, %6;\n\tadd.u32 b4, b3, %6;\n\t"
+        "add.u32 b5, b4, %6;\n\tadd.u32 b6, b5, %6;\n\tadd.u32 b7, b6, %6;\n\tadd.u32 b8, b7, %6;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "add.u32 ta, alo, 0;\n\tadd.u32 tb, blo, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, p;\n\t"
+        "add.u32 ta, alo, 2;\n\tadd.u32 tb, blo, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 4;\n\tadd.u32 tb, b1, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 6;\n\tadd.u32 tb, b1, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 8;\n\tadd.u32 tb, b2, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 10;\n\tadd.u32 tb, b2, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 0;\n\tadd.u32 tb, b3, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 2;\n\tadd.u32 tb, b3, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 4;\n\tadd.u32 tb, b4, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 6;\n\tadd.u32 tb, b4, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 8;\n\tadd.u32 tb, b5, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 10;\n\tadd.u32 tb, b5, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 0;\n\tadd.u32 tb, b6, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 2;\n\tadd.u32 tb, b6, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 4;\n\tadd.u32 tb, b7, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 6;\n\tadd.u32 tb, b7, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 8;\n\tadd.u32 tb, b8, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 10;\n\tadd.u32 tb, b8, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "}\n"
+        ::"r"(d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(arow), "r"(btap)
+        : "memory");
+}
+
+template <>
+__device__ __forceinline__ void mma_3x3_chunk<4>(uint32_t d, uint64_t da, uint64_t db, uint32_t arow, uint32_t btap,
+                                                 uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t.reg .b32 alo, ahi, blo, bhi, a1, a2, b1, b2, b3, b4, b5, b6, b7, b8, ta, tb;\n\t.reg .b64 A, B;\n\t"
+        "mov.b64 {alo, ahi}, %1;\n\tmov.b64 {blo, bhi}, %2;\n\t"
+        "add.u32 a1, alo, %5;\n\tadd.u32 a2, a1, %5;\n\t"
+        "add.u32 b1, blo, %6;\n\tadd.u32 b2, b1, %6;\n\tadd.u32 b3, b2, %6;\n\tadd.u32 b4, b3, %6;\n\t"
+        "add.u32 b5, b4, %6;\n\tadd.u32 b6, b5, %6;\n\tadd.u32 b7, b6, %6;\n\tadd.u32 b8, b7, %6;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "add.u32 ta, alo, 0;\n\tadd.u32 tb, blo, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, p;\n\t"
+        "add.u32 ta, alo, 2;\n\tadd.u32 tb, blo, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 4;\n\tadd.u32 tb, blo, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 6;\n\tadd.u32 tb, blo, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 8;\n\tadd.u32 tb, b1, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 10;\n\tadd.u32 tb, b1, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 12;\n\tadd.u32 tb, b1, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 14;\n\tadd.u32 tb, b1, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 16;\n\tadd.u32 tb, b2, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 18;\n\tadd.u32 tb, b2, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 20;\n\tadd.u32 tb, b2, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, alo, 22;\n\tadd.u32 tb, b2, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 0;\n\tadd.u32 tb, b3, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 2;\n\tadd.u32 tb, b3, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 4;\n\tadd.u32 tb, b3, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 6;\n\tadd.u32 tb, b3, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 8;\n\tadd.u32 tb, b4, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 10;\n\tadd.u32 tb, b4, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 12;\n\tadd.u32 tb, b4, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 14;\n\tadd.u32 tb, b4, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 16;\n\tadd.u32 tb, b5, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 18;\n\tadd.u32 tb, b5, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 20;\n\tadd.u32 tb, b5, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a1, 22;\n\tadd.u32 tb, b5, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 0;\n\tadd.u32 tb, b6, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 2;\n\tadd.u32 tb, b6, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 4;\n\tadd.u32 tb, b6, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 6;\n\tadd.u32 tb, b6, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 8;\n\tadd.u32 tb, b7, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 10;\n\tadd.u32 tb, b7, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 12;\n\tadd.u32 tb, b7, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 14;\n\tadd.u32 tb, b7, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 16;\n\tadd.u32 tb, b8, 0;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 18;\n\tadd.u32 tb, b8, 2;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 20;\n\tadd.u32 tb, b8, 4;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "add.u32 ta, a2, 22;\n\tadd.u32 tb, b8, 6;\n\t"
+        "mov.b64 A, {ta, ahi};\n\tmov.b64 B, {tb, bhi};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], A, B, %3, 1;\n\t"
+        "}\n"
+        ::"r"(d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(arow), "r"(btap)
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_commit_elect(uint32_t bar) {
     asm volatile(
         "{\n\t.reg .pred e;\n\t"
@@ -1093,18 +1338,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     mma_chunk_elect<CB / 32>(d, da0, bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step, idesc,
                                              ka != 0 ? 1u : 0u);
                 } else if (MODE == 1) {
-                    // 3x3 taps (mode 1 is planned only for 3x3 convs and the 1x1 stem GEMM), fully unrolled
-                    uint64_t da_row = da0;
-                    uint64_t db = bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step;
-                    uint32_t acc = ka != 0 ? 1u : 0u;
-#pragma unroll
-                    for (int i = 0; i < 3; ++i, da_row += a_row_step) {
-#pragma unroll
-                        for (int j = 0; j < 3; ++j, db += b_tap_step) {
-                            mma_chunk_elect<CB / 32>(d, da_row + static_cast<uint64_t>(j * (CB >> 4)), db, idesc, acc);
-                            acc = 1u;
-                        }
-                    }
+                    // 3x3 taps (mode 1 is planned only for 3x3 convs and the 1x1 stem GEMM): the chunk's
+                    // 9 x CB/32 MMAs from one asm block
+                    mma_3x3_chunk<CB / 32>(d, da0, bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step,
+                                           static_cast<uint32_t>(a_row_step), static_cast<uint32_t>(b_tap_step), idesc,
+                                           ka != 0 ? 1u : 0u);
                 } else {
                     const uint64_t db = bdesc0 + static_cast<uint64_t>(g.b_resident ? ka : s) * b_chunk_step;
                     mma_chunk_elect<CB / 32>(d, da0, db, idesc, ka != 0 ? 1u : 0u);
