@@ -42,7 +42,7 @@ def config_info(cfg: int) -> dict:
     c = mg.CONFIGS[cfg]
     mv2 = c["model"] == "mobilenet_v2"
     prec = "w4w8a8_mixed" if c.get("mixed") else "w8a8"
-    return {"metric": METRIC_MV2 if mv2 else METRIC, "batch": c["batch"], "passes": 3 if c.get("passes") else 0,
+    return {"metric": METRIC_MV2 if mv2 else METRIC, "batch": c["batch"], "passes": 7 if c.get("passes") else 0,
             "name": f"{'mobilenet_v2' if mv2 else 'resnet18_' + c['stem']}_{prec}"}
 
 
@@ -431,6 +431,21 @@ def main():
                                 "ms": p["ms"], "tops": 2.0 * p["macs"] / (p["ms"] / 1e3) / 1e12,
                                 "frac": 2.0 * p["macs"] / (p["ms"] / 1e3) / 1e12 / int8_peak}
                                for p in tc if p["ms"] > 0]}
+    # memory-bound launches (depthwise convs, maxpool, pooling head): algorithmic bytes (codes
+    # read once, codes / fp32 written once, weights once) over their device time, against the
+    # measured HBM copy bandwidth
+    memk = [p for p in prof if p["kind"] in (2, 3, 4) and p["ms"] > 0]
+    roofline_hbm = None
+    if memk:
+        m_ms = sum(p["ms"] for p in memk)
+        m_gbs = sum(p["bytes"] for p in memk) / (m_ms / 1e3) / 1e9
+        names = {2: "depthwise", 3: "maxpool", 4: "head"}
+        roofline_hbm = {"bound": "hbm", "achieved": m_gbs, "peak": hbm, "unit": "GB/s", "frac": m_gbs / hbm,
+                        "kernel": "dw3x3_kernel / dw_conv_kernel (depthwise), maxpool_kernel, head_kernel",
+                        "peak_source": f"hbm_gbs of {src} MEASURED_PEAKS.json", "ms": m_ms,
+                        "per_launch": [{"step": p["step"], "kind": names[p["kind"]], "ms": p["ms"],
+                                        "gbs": p["bytes"] / (p["ms"] / 1e3) / 1e9,
+                                        "frac": p["bytes"] / (p["ms"] / 1e3) / 1e9 / hbm} for p in memk]}
     wb = eng.weight_bytes()
 
     # ---- end to end through the C-ABI host-buffer forwards (H2D + graph + D2H every step).
@@ -443,10 +458,17 @@ def main():
 
     windows = [(t_wall0, t_wall1)]   # host-time windows of the timed regions (clock samples)
 
-    def host_loop(pipelined: bool) -> float:
+    # 8-bit pixels (CIFAR-10 record format without the label byte): decode + normalise +
+    # quantize run in the stem kernel, 1 byte per input value over PCIe instead of 4
+    ph = torch.from_numpy(np.random.default_rng(1234 + rank).integers(0, 256, size=(B, 3, 32, 32),
+                                                                        dtype=np.uint8)).pin_memory()
+
+    def host_loop(mode: str) -> float:
+        pipelined = mode == "async"
         for _ in range(2):
             eng.forward_host_ptr(xh.data_ptr(), B, 3, 32, 32, lh.data_ptr())
             eng.forward_async(xh.data_ptr(), B, lh.data_ptr())
+            eng.forward_u8_async(ph.data_ptr(), B, 0, lh.data_ptr())
         eng.sync()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -456,6 +478,8 @@ def main():
         for _ in range(a.steps):
             if pipelined:
                 eng.forward_async(xh.data_ptr(), B, lh.data_ptr())
+            elif mode == "u8":
+                eng.forward_u8_async(ph.data_ptr(), B, 0, lh.data_ptr())
             else:
                 eng.forward_host_ptr(xh.data_ptr(), B, 3, 32, 32, lh.data_ptr())
         eng.sync()
@@ -464,17 +488,21 @@ def main():
         windows.append((w0, time.time()))
         return max_over_ranks(e0.elapsed_time(e1), "cuda")
 
-    ems = host_loop(True)
-    ems_sync = host_loop(False)
+    ems = host_loop("async")
+    ems_sync = host_loop("sync")
+    ems_u8 = host_loop("u8")
     clk = clocks.stop(windows)
-    clk["windows"] = "the device-timed loop and both e2e loops"
+    clk["windows"] = "the device-timed loop and the three e2e loops"
     roofline["peak_i8_issue_rate"] = (8192 * sms * clk["sm_mhz"] * 1e6 * 2 / 1e12) if clk.get("sm_mhz") else None
     if roofline["peak_i8_issue_rate"]:
         roofline["frac_of_i8_issue_rate"] = achieved / roofline["peak_i8_issue_rate"]
     e2e = {"value": world * B * a.steps / (ems / 1e3), "unit": "images/s",
            "h2d_bytes_per_step": B * 3 * 32 * 32 * 4, "d2h_bytes_per_step": B * 10 * 4,
            "call": "ptq8_engine_forward_async (pinned host buffers; step k+1's H2D overlaps step k's forward)",
-           "sync_call_value": world * B * a.steps / (ems_sync / 1e3)}
+           "sync_call_value": world * B * a.steps / (ems_sync / 1e3),
+           "u8_input": {"value": world * B * a.steps / (ems_u8 / 1e3), "h2d_bytes_per_step": B * 3 * 32 * 32,
+                        "call": "ptq8_engine_forward_u8_async (8-bit CIFAR-10 pixels; normalisation and "
+                                "quantization in the stem kernel)"}}
 
     if rank == 0:
         line = {"metric": info["metric"], "value": value, "unit": "images/s", "n_gpus": world, "steps": a.steps,
@@ -483,7 +511,7 @@ def main():
                 "config": {"workload": f"{info['name']}_b{B} (BASELINE configs[{a.config}])", "batch_per_gpu": B,
                            "parallelism": f"dp{world}", "l2": "inputs and activations larger than L2 (>10 GB/step)",
                            "logits_gather": "nccl all_gather per step (side stream)" if world > 1 else "none"},
-                "roofline": roofline, "e2e": e2e, "clocks": clk, "weights": wb,
+                "roofline": roofline, "roofline_hbm": roofline_hbm, "e2e": e2e, "clocks": clk, "weights": wb,
                 "gpu_launches": a.steps * eng.n_launches()}
         if multi is not None:
             line["multi_gpu"] = multi

@@ -32,6 +32,10 @@ extern "C" {
 /* graph passes (ptq8_engine_build `passes` bit mask) */
 #define PTQ8_PASS_CENTER_TAP 1 /* 07-tensorrt-deploy/scripts/push_optimize_onnx.py:36-93 */
 #define PTQ8_PASS_DECOMPOSE 2  /* 07-tensorrt-deploy/scripts/push_decompose.py:99-202  */
+/* generalised positional decomposition: per-position sub-convs of convs whose output
+ * positions read different kernel slices (push_decompose.py:50-80 computes the slices; its
+ * decompose() declines such geometries); taps that only read padding are skipped */
+#define PTQ8_PASS_POSITIONAL 4
 
 /* activation range modes (06-gpu-int8/cpp/ptq_quant.h:163) */
 #define PTQ8_ACT_ABSMAX 0
@@ -158,6 +162,33 @@ int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float*
 /* Device-pointer forward (fp32 NCHW input, fp32 [n][fc_out] logits); enqueued
  * on the engine stream, not synchronized. */
 int ptq8_engine_forward_device(ptq8_engine* e, const float* x_dev, int n, float* logits_dev);
+/* ---- 8-bit pixel input (CIFAR-10 records) ----------------------------------
+ * The reference decodes CIFAR-10 records and normalises them on the host, then
+ * uploads fp32 (ref_e2e.py:261-276; main.cpp:178-198,245-261).  These calls upload the
+ * 8-bit pixels (1 byte per value instead of 4) and the stem kernel does the
+ * normalisation and the exact quantization on the device: the same network input
+ * codes, bit for bit, as the reference's fp32 path, given the same normalisation.
+ * Pixels are [n][c][h][w] bytes per image; image i starts at x + i * record_bytes
+ * (record_bytes 0: c*h*w, packed; a raw CIFAR-10 batch file is x = file + 1,
+ * record_bytes = 3073, skipping each record's label byte).  At most 4 channels. */
+#define PTQ8_NORM_DIV 0 /* x = (px - mean*255) / (std*255): ref_e2e.py:272-274 (the default) */
+#define PTQ8_NORM_MUL 1 /* x = ((px/255)*255 - mean*255) * (1/(std*255)): main.cpp:245-261 */
+/* Normalisation of 8-bit input (mode PTQ8_NORM_*; mean/std: float[c], or both NULL for the
+ * CIFAR-10 constants of main.cpp:25-26).  Every operation in float32, rounded to nearest.
+ * Drops captured 8-bit-input graphs. */
+int ptq8_engine_set_input_norm(ptq8_engine* e, int mode, const float* mean, const float* std_);
+/* Int8Engine::forward (int8_engine.cuh:429) from 8-bit host pixels: H2D of the pixels,
+ * the forward as one CUDA graph, D2H of the logits, synchronize. */
+int ptq8_engine_forward_u8(ptq8_engine* e, const uint8_t* x_host, int n, size_t record_bytes, float* logits_host);
+/* Pipelined form of ptq8_engine_forward_u8, with the semantics of ptq8_engine_forward_async
+ * (same two input slots and copy stream; wait with ptq8_engine_sync). */
+int ptq8_engine_forward_u8_async(ptq8_engine* e, const uint8_t* x_host, int n, size_t record_bytes,
+                                 float* logits_host);
+/* Device-pointer form (8-bit pixels on the device, fp32 logits [n][fc_out]); enqueued on
+ * the engine stream, not synchronized. */
+int ptq8_engine_forward_device_u8(ptq8_engine* e, const uint8_t* x_dev, int n, size_t record_bytes,
+                                  float* logits_dev);
+
 /* Engine-resident buffers: callers may write inputs straight into the input
  * buffer and run ptq8_engine_run() with no copies. */
 float* ptq8_engine_input_buffer(ptq8_engine* e);

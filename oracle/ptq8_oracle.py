@@ -22,6 +22,8 @@ It restates, in numpy, the reference's integer-simulated forward:
                               09-ptq-toolkit/ptq_toolkit/export/topoblocks.py:181-220 and
                               06-gpu-int8/cpp/ref_e2e.py:208-256
 * ``maxpool3x3s2p1``       <- 06-gpu-int8/cpp/ref_e2e.py:192-203
+* ``normalize_u8``         <- 06-gpu-int8/cpp/ref_e2e.py:261-276 (mode 0) and
+                              06-gpu-int8/cpp/main.cpp:25-26,245-261 (mode 1)
 * PTQ2 / PTQW / PTQC readers <- topoblocks.py:17-35,247-267, ref_e2e.py:42-87
 
 Parity pin: ``tests/golden/make_golden.py`` runs the reference's own
@@ -220,6 +222,29 @@ def maxpool3x3s2p1(x: np.ndarray) -> np.ndarray:
         xp, shape=(N, C, OH, OW, 3, 3),
         strides=(s[0], s[1], s[2] * 2, s[3] * 2, s[2], s[3]), writeable=False)
     return view.max(axis=(-1, -2)).astype(np.float32)
+
+
+# --------------------------------------------------------------------------- 8-bit input
+
+CIFAR_MEAN = (0.4914, 0.4822, 0.4465)   # main.cpp:25, ref_e2e.py:272
+CIFAR_STD = (0.2470, 0.2435, 0.2616)    # main.cpp:26, ref_e2e.py:273
+
+
+def normalize_u8(px: np.ndarray, mode: int = 0, mean=CIFAR_MEAN, std=CIFAR_STD) -> np.ndarray:
+    """8-bit pixels [N][C][H][W] -> the fp32 network input, every step in float32.
+
+    mode 0 (ref_e2e.py:271-275): x = (px - mean*255) / (std*255).
+    mode 1 (main.cpp:245-261):   p = px / 255; x = (p*255 - mean*255) * (1 / (std*255)).
+    """
+    p = np.asarray(px).astype(np.float32)
+    c = p.shape[1]
+    m = (np.asarray(mean, dtype=np.float32) * np.float32(255.0)).reshape(1, c, 1, 1)
+    sd = (np.asarray(std, dtype=np.float32) * np.float32(255.0)).reshape(1, c, 1, 1)
+    if mode == 0:
+        return ((p - m) / sd).astype(np.float32)
+    inv = np.float32(1.0) / sd
+    q = p / np.float32(255.0)
+    return (((q * np.float32(255.0)) - m) * inv).astype(np.float32)
 
 
 # --------------------------------------------------------------------------- model files

@@ -45,6 +45,27 @@ std::string strf(const char* f, ...) {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
+// Normalisation constants of 8-bit CIFAR-10 pixels, computed in float32 as the
+// reference's input paths compute them: m = mean * 255; kNormDiv: d = std * 255
+// (ref_e2e.py:272-274, numpy float32); kNormMul: d = 1 / (std * 255)
+// (main.cpp:25-26,257-258).
+U8Norm make_norm(int mode, const float* mean, const float* sd, int c) {
+    U8Norm nm{};
+    nm.mode = mode;
+    for (int k = 0; k < c; ++k) {
+        const volatile float m = mean[k] * 255.0f;   // each float32 operation rounded on its own
+        const volatile float d = sd[k] * 255.0f;
+        nm.m[k] = m;
+        nm.d[k] = mode == kNormMul ? 1.0f / d : d;
+    }
+    return nm;
+}
+
+U8Norm cifar_norm(int mode) {
+    static const float kMean[3] = {0.4914f, 0.4822f, 0.4465f}, kStd[3] = {0.2470f, 0.2435f, 0.2616f};
+    return make_norm(mode, kMean, kStd, 3);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -141,6 +162,9 @@ struct ConvQ {   // quantized conv after graph passes
     std::vector<float> bias;
     // positional decomposition: output channel c' = pos*cout_orig + c (NHWC == D2S DCR)
     int view_oh = 0, view_ow = 0;   // >0 when the conv runs as a 1x1-output GEMM
+    // generalised positional decomposition: per-position sub-convs (each output position of
+    // TN images is one M tile that multiplies only its in-bounds taps)
+    bool pos_tiles = false;
 };
 
 }  // namespace
@@ -175,6 +199,11 @@ struct ptq8_engine {
     // copy stream, per-slot events, next slot; graphs are keyed by batch * 2 + slot
     float* d_input2 = nullptr;
     const float* cur_input = nullptr;   // the input the stem reads while a forward is enqueued
+    // 8-bit pixel input (ptq8_engine_forward_u8*): two lazily allocated slots [max_batch][c*h*w],
+    // the normalisation the stem applies, and the slot a forward being enqueued reads
+    uint8_t* d_input_u8[2] = {nullptr, nullptr};
+    const uint8_t* cur_input_u8 = nullptr;
+    U8Norm u8_norm = cifar_norm(kNormDiv);
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_staged[2] = {nullptr, nullptr}, ev_free[2] = {nullptr, nullptr};
     int async_slot = 0;
@@ -328,6 +357,45 @@ bool decompose(ConvQ& cq, int H, int W, std::string* note) {
     c.kw = tw;
     c.sh = c.sw = 1;
     c.ph = c.pw = 0;
+    return true;
+}
+
+// Generalised positional decomposition: the per-position sub-convs of a conv whose
+// output positions read different kernel slices (07-tensorrt-deploy/scripts/
+// push_decompose.py:50-80 computes the slice per position; its decompose() needs every
+// position to read the whole input with the same slice, which the CIFAR-stem ResNet-18's
+// 8x8 and 4x4 maps never do).  Output position (i, j) is the GEMM of the images' codes
+// under kernel rows [lo_h(i), hi_h(i)] and columns [lo_w(j), hi_w(j)] -- the taps that
+// read inside the input -- with the same codes' weights: the dropped taps multiply padding
+// code 0, so every int32 accumulator is unchanged.  The engine runs each position as its
+// own M tiles (TN images at one position; mode 0) and skips the dropped taps' K chunks.
+// Applied to output maps of at most 64 positions where the dropped taps are at least 5 %
+// of the conv's MACs.
+bool positional(ConvQ& cq, int H, int W, std::string* note) {
+    const ConvSpec& c = cq.spec;
+    if (c.groups != 1 || c.kh == 1 || c.kw == 1 || cq.view_oh > 0) return false;
+    const int OH = (H + 2 * c.ph - c.kh) / c.sh + 1, OW = (W + 2 * c.pw - c.kw) / c.sw + 1;
+    // larger maps keep their row-block tiles (the halo-block pipeline of stride-1 convs)
+    if (OH < 1 || OW < 1 || OH * OW > 64) return false;
+    long long full = 0, kept = 0;
+    int classes_h = 0, classes_w = 0, prev_h = -1, prev_w = -1;
+    for (int i = 0; i < OH; ++i) {
+        const int lo = std::max(0, c.ph - c.sh * i), hi = std::min(c.kh - 1, H - 1 + c.ph - c.sh * i);
+        if (lo > hi) return false;
+        if (lo * 64 + hi != prev_h) { ++classes_h; prev_h = lo * 64 + hi; }
+        for (int j = 0; j < OW; ++j) {
+            const int lw = std::max(0, c.pw - c.sw * j), hw = std::min(c.kw - 1, W - 1 + c.pw - c.sw * j);
+            if (lw > hw) return false;
+            if (i == 0 && lw * 64 + hw != prev_w) { ++classes_w; prev_w = lw * 64 + hw; }
+            full += (long long)c.kh * c.kw;
+            kept += (long long)(hi - lo + 1) * (hw - lw + 1);
+        }
+    }
+    if ((full - kept) * 20 < full) return false;   // under 5 % of the MACs read padding
+    cq.pos_tiles = true;
+    const long long macs = (long long)c.cout * c.cin;
+    *note = strf("positional %dx%d s%d on %dx%d -> %d position classes (%dx%d), MACs %lld -> %lld per image",
+                 c.kh, c.kw, c.sh, H, W, classes_h * classes_w, classes_h, classes_w, full * macs, kept * macs);
     return true;
 }
 
@@ -508,7 +576,6 @@ int plan(ptq8_engine* e) {
     e->vals.clear();
     e->steps.clear();
     e->conv_step.assign(m.convs.size(), -1);
-    e->passes_log.clear();
 
     // --- shapes of every conv input, computed along the topology
     std::vector<int> in_h(m.convs.size(), 0), in_w(m.convs.size(), 0);
@@ -699,9 +766,23 @@ template <int CBI, int MODE>
 void fill_nout() { fill_res<CBI, MODE, 0>(); fill_res<CBI, MODE, 1>(); fill_res<CBI, MODE, 2>(); }
 template <int CBI>
 void fill_mode() { fill_nout<CBI, 0>(); fill_nout<CBI, 1>(); }
+// The same compile-time N tile epilogue for the 64-channel residual convs of the halo-block
+// pipeline: [code outputs 1/2][residual load][fp32 output][aux GEMM identity].
+void* g_conv_fast_res_table[2][2][2][2];
+template <int NOUT, int RES, int F32, int AUX>
+void fill_fast_res() {
+    g_conv_fast_res_table[NOUT - 1][RES][F32][AUX] =
+        reinterpret_cast<void*>(&conv_tc_kernel<64, 1, NOUT, (RES != 0 || AUX != 0), F32 != 0, AUX != 0, 64>);
+}
+// Whether the 64-channel residual convs use that epilogue (grouped warps, unrolled
+// 64-column rows) instead of the column-stationary one.
+constexpr bool kFastResidual = false;
+
 void fill_table() {
     static bool done = false;
     if (done) return;
+    fill_fast_res<1, 1, 0, 0>(); fill_fast_res<2, 1, 0, 0>(); fill_fast_res<1, 1, 1, 0>(); fill_fast_res<2, 1, 1, 0>();
+    fill_fast_res<1, 0, 1, 1>(); fill_fast_res<2, 0, 1, 1>(); fill_fast_res<1, 0, 0, 1>(); fill_fast_res<2, 0, 0, 1>();
     fill_mode<0>();
     fill_mode<1>();
     fill_mode<2>();
@@ -919,11 +1000,15 @@ int finalize(ptq8_engine* e, int max_batch) {
             continue;
         }
         tile_shape(max_batch, st.oh, st.ow, &st.TW, &st.TH, &st.TN);
+        if (cq.pos_tiles) {   // one output position of 128 images per M tile
+            st.TW = st.TH = 1;
+            st.TN = 128;
+        }
         st.n_kchunks = st.kind == K_STEM_IM2COL ? st.kpad / st.cb : st.kh * st.kw * (cpad / st.cb);
         // mode 1: stride-1 "same" convs read one halo block per tile (needs resident weights)
         st.mode = 0;
         // (the kernel's halo-block MMA loop is compiled for 3x3)
-        if (st.kind == K_TC && cq.view_oh == 0 && st.kh == 3 && st.kw == 3 && st.sh == 1 && st.sw == 1 &&
+        if (st.kind == K_TC && cq.view_oh == 0 && !cq.pos_tiles && st.kh == 3 && st.kw == 3 && st.sh == 1 && st.sw == 1 &&
             st.ph == (st.kh - 1) / 2 && st.pw == st.ph && st.ph <= 1 && st.oh == st.ih && st.ow == st.iw &&
             st.oh * st.ow >= 64) {
             const int wp = st.iw + 2;
@@ -1075,7 +1160,13 @@ int finalize(ptq8_engine* e, int max_batch) {
             st.fast = (st.kind == K_TC || st.kind == K_STEM_IM2COL) && st.mode == 1 && st.n_ntiles == 1 &&
                       e->q[st.conv].view_oh == 0 && st.oc == st.bn && fast_index(st.cb, st.bn) >= 0 &&
                       nout >= 1 && nout <= 2 && !res && !f32 && st.aux_src < 0;
-            if (st.fast) {
+            const bool fast_res = kFastResidual && !st.fast && st.kind == K_TC && st.mode == 1 && st.n_ntiles == 1 &&
+                                  e->q[st.conv].view_oh == 0 && st.oc == 64 && st.bn == 64 && st.cb == 64 &&
+                                  nout >= 1 && nout <= 2 && (res || f32 || st.aux_src >= 0);
+            if (fast_res) {
+                st.fast = true;
+                st.kfn = g_conv_fast_res_table[nout - 1][st.aux_src >= 0 ? 0 : res][f32][st.aux_src >= 0 ? 1 : 0];
+            } else if (st.fast) {
                 st.kfn = g_conv_fast_table[fast_index(st.cb, st.bn)][nout - 1];
             } else if (st.aux_src >= 0) {
                 if (nout < 1 || nout > 2) return e->fail(strf("conv[%d]: stem identity fusion needs 1-2 code outputs", st.conv));
@@ -1245,10 +1336,15 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         const int bands = (st.oh + rows - 1) / rows;
         const size_t band_bytes =
             (((size_t)c.cin * ((rows - 1) * c.sh + c.kh) * band_w + 15) & ~(size_t)15) + (size_t)st.kpad * sizeof(int);
-        launch_pdl(stem_im2col_kernel, dim3(n * bands), dim3(256), band_bytes, s,
-                   e->cur_input ? e->cur_input : (const float*)e->d_input,
-                   st.d_im2col, n, c.cin, st.ih, st.iw, st.oh, st.ow, c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad, rows,
-                   (float)(1.0 / st.s_in), st.s_in);
+        if (e->cur_input_u8)   // 8-bit pixels, normalised and quantized through a per-CTA code table
+            launch_pdl(stem_im2col_kernel<true>, dim3(n * bands), dim3(256), band_bytes + (size_t)c.cin * 256, s,
+                       (const void*)e->cur_input_u8, st.d_im2col, n, c.cin, st.ih, st.iw, st.oh, st.ow, c.kh, c.kw,
+                       c.sh, c.sw, c.ph, c.pw, st.kpad, rows, (float)(1.0 / st.s_in), st.s_in, e->u8_norm);
+        else
+            launch_pdl(stem_im2col_kernel<false>, dim3(n * bands), dim3(256), band_bytes, s,
+                       (const void*)(e->cur_input ? e->cur_input : (const float*)e->d_input), st.d_im2col, n, c.cin,
+                       st.ih, st.iw, st.oh, st.ow, c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, st.kpad, rows,
+                       (float)(1.0 / st.s_in), st.s_in, e->u8_norm);
     }
     ConvGeom g{};
     g.mode = st.mode;
@@ -1267,6 +1363,9 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         g.KW = st.kw; g.SH = st.sh; g.SW = st.sw; g.PH = st.ph; g.PW = st.pw;
         g.coord_off = 1;
         g.n_cchunks = e->vals[st.in_val].ldq / st.cb;
+        g.pos_tiles = st.mode == 0 && e->q[st.conv].pos_tiles ? 1 : 0;
+        g.IH = st.ih;
+        g.IW = st.iw;
     }
     if (st.mode == 1) {
         // the bordered grid of the output (= of the input for stride-1 "same" convs; the stem's
@@ -1389,8 +1488,9 @@ void step_work(const ptq8_engine* e, int n, size_t si, double* macs, double* byt
 }
 
 // The CUDA graph of one forward at batch n reading input slot `slot` (0: d_input,
-// 1: d_input2), captured on first use, then cached.
-int graph_for(ptq8_engine* e, int n, cudaGraphExec_t* out, int slot = 0) {
+// 1: d_input2; u8: the 8-bit pixel slots d_input_u8[slot]), captured on first use,
+// then cached.
+int graph_for(ptq8_engine* e, int n, cudaGraphExec_t* out, int slot = 0, bool u8 = false) {
     if (!e->planned) {
         int rc = finalize(e, std::max(n, e->max_batch > 0 ? e->max_batch : n));
         if (rc) return rc;
@@ -1398,15 +1498,18 @@ int graph_for(ptq8_engine* e, int n, cudaGraphExec_t* out, int slot = 0) {
     if (n <= 0 || n > e->max_batch)
         return e->fail(strf("batch %d outside [1, %d] (alloc_scratch sets the maximum)", n, e->max_batch));
     if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
-    const int key = n * 2 + slot;
+    if (u8 && !e->d_input_u8[slot]) return e->fail("8-bit input slot not allocated");
+    const int key = n * 4 + slot + (u8 ? 2 : 0);
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         cudaGraph_t g;
         if (!e->cuda_ok(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture"))
             return PTQ8_ERR_CUDA;
         e->cur_input = slot ? e->d_input2 : e->d_input;
+        e->cur_input_u8 = u8 ? e->d_input_u8[slot] : nullptr;
         int rc = enqueue(e, n);
         e->cur_input = nullptr;
+        e->cur_input_u8 = nullptr;
         cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
         if (rc) return rc;
         if (!e->cuda_ok(ce, "end capture")) return PTQ8_ERR_CUDA;
@@ -1788,6 +1891,7 @@ int ptq8_engine_build(ptq8_engine* e, const ptq8_model* mm, int w_bits, int a_bi
             cq.bias = c.bias;
         }
         // graph passes run on the quantized layers (codes + scales), so they are exact
+        e->passes_log.clear();
         if (passes) {
             int h = conv_out_dim(e->in_h, m.convs[0].kh, m.convs[0].sh, m.convs[0].ph);
             int w = conv_out_dim(e->in_w, m.convs[0].kw, m.convs[0].sw, m.convs[0].pw);
@@ -1799,6 +1903,7 @@ int ptq8_engine_build(ptq8_engine* e, const ptq8_model* mm, int w_bits, int a_bi
                     bool done = false;
                     if (passes & PTQ8_PASS_CENTER_TAP) done = center_tap(e->q[ci], ih, iw, &note);
                     if (!done && (passes & PTQ8_PASS_DECOMPOSE)) done = decompose(e->q[ci], ih, iw, &note);
+                    if (!done && (passes & PTQ8_PASS_POSITIONAL)) done = positional(e->q[ci], ih, iw, &note);
                     e->passes_log.push_back(strf("conv[%d] in %dx%d: %s", ci, ih, iw, done ? note.c_str() : "unchanged"));
                 };
                 if (b.ds >= 0) try_conv(b.ds, h, w);
@@ -1961,6 +2066,25 @@ int ptq8_engine_forward(ptq8_engine* e, const float* x_host, int n, int c, int h
     return ptq8_engine_check_device_error(e);
 }
 
+namespace {
+
+// The pipelined forwards' copy stream and per-slot events, created on first use.
+int ensure_copy_stream(ptq8_engine* e) {
+    if (e->copy_stream) return PTQ8_OK;
+    if (!e->cuda_ok(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking), "copy stream"))
+        return PTQ8_ERR_CUDA;
+    for (int k = 0; k < 2; ++k)
+        if (!e->cuda_ok(cudaEventCreateWithFlags(&e->ev_staged[k], cudaEventDisableTiming), "event") ||
+            !e->cuda_ok(cudaEventCreateWithFlags(&e->ev_free[k], cudaEventDisableTiming), "event") ||
+            // work already queued on the engine stream (a forward_device or run graph
+            // reading slot 0) must finish before the first pipelined copy overwrites a slot
+            !e->cuda_ok(cudaEventRecord(e->ev_free[k], e->stream), "record free"))
+            return PTQ8_ERR_CUDA;
+    return PTQ8_OK;
+}
+
+}  // namespace
+
 int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float* logits_host) {
     try {
         if (!e || !x_host || !logits_host) return PTQ8_ERR_INVALID;
@@ -1971,17 +2095,8 @@ int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float*
         if (n <= 0 || n > e->max_batch) return e->fail(strf("batch %d outside [1, %d]", n, e->max_batch));
         if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
         const size_t in_bytes = (size_t)n * e->in_c * e->in_h * e->in_w * sizeof(float);
-        if (!e->copy_stream) {
-            if (!e->cuda_ok(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking), "copy stream"))
-                return PTQ8_ERR_CUDA;
-            for (int k = 0; k < 2; ++k)
-                if (!e->cuda_ok(cudaEventCreateWithFlags(&e->ev_staged[k], cudaEventDisableTiming), "event") ||
-                    !e->cuda_ok(cudaEventCreateWithFlags(&e->ev_free[k], cudaEventDisableTiming), "event") ||
-                    // work already queued on the engine stream (a forward_device or run graph
-                    // reading slot 0) must finish before the first pipelined copy overwrites a slot
-                    !e->cuda_ok(cudaEventRecord(e->ev_free[k], e->stream), "record free"))
-                    return PTQ8_ERR_CUDA;
-        }
+        int rc = ensure_copy_stream(e);
+        if (rc) return rc;
         if (!e->d_input2 &&
             !e->dalloc(&e->d_input2, (size_t)e->max_batch * e->in_c * e->in_h * e->in_w * sizeof(float),
                        "alloc second input slot"))
@@ -1989,7 +2104,7 @@ int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float*
         const int slot = e->async_slot;
         float* dst = slot ? e->d_input2 : e->d_input;
         cudaGraphExec_t ge;
-        int rc = graph_for(e, n, &ge, slot);
+        rc = graph_for(e, n, &ge, slot);
         if (rc) return rc;
         // the slot is free once the forward that last read it has run (a never-recorded
         // event is no dependency)
@@ -2007,6 +2122,152 @@ int ptq8_engine_forward_async(ptq8_engine* e, const float* x_host, int n, float*
         return PTQ8_OK;
     } catch (const std::exception& ex) {
         return e ? e->fail(strf("forward_async: %s", ex.what()), PTQ8_ERR_CUDA) : PTQ8_ERR_CUDA;
+    }
+}
+
+int ptq8_engine_set_input_norm(ptq8_engine* e, int mode, const float* mean, const float* std_) {
+    if (!e) return PTQ8_ERR_INVALID;
+    if (mode != PTQ8_NORM_DIV && mode != PTQ8_NORM_MUL)
+        return e->fail(strf("input normalisation mode %d: must be %d (div) or %d (mul)", mode, PTQ8_NORM_DIV,
+                            PTQ8_NORM_MUL));
+    if ((mean == nullptr) != (std_ == nullptr)) return e->fail("mean and std: both given or both NULL");
+    if (e->in_c > 4) return e->fail(strf("8-bit input: at most 4 channels (engine input has %d)", e->in_c));
+    U8Norm nm;
+    if (!mean) {
+        if (e->in_c != 3) return e->fail("the CIFAR-10 constants need a 3-channel input");
+        nm = cifar_norm(mode);
+    } else {
+        for (int k = 0; k < e->in_c; ++k)
+            if (!std::isfinite(mean[k]) || !std::isfinite(std_[k]) || !(std_[k] > 0.0f))
+                return e->fail(strf("channel %d: mean must be finite and std finite and positive", k));
+        nm = make_norm(mode, mean, std_, e->in_c);
+        for (int k = 0; k < e->in_c; ++k)
+            if (!std::isfinite(nm.m[k]) || !std::isfinite(nm.d[k]) || !(nm.d[k] > 0.0f))
+                return e->fail(strf("channel %d: normalisation constants overflow float32", k));
+    }
+    // graphs of 8-bit forwards carry the constants as kernel parameters
+    if (e->stream && !e->cuda_ok(cudaStreamSynchronize(e->stream), "sync")) return PTQ8_ERR_CUDA;
+    for (auto it = e->graphs.begin(); it != e->graphs.end();) {
+        if (it->first & 2) {
+            cudaGraphExecDestroy(it->second);
+            it = e->graphs.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    e->u8_norm = nm;
+    return PTQ8_OK;
+}
+
+namespace {
+
+// Checks shared by the 8-bit input forwards; allocates 8-bit input slot `slot` on first use.
+int u8_prepare(ptq8_engine* e, int n, size_t record_bytes, int slot, size_t* img_bytes) {
+    if (!e->planned) {
+        int rc = finalize(e, std::max(n, e->max_batch));
+        if (rc) return rc;
+    }
+    if (n <= 0 || n > e->max_batch) return e->fail(strf("batch %d outside [1, %d]", n, e->max_batch));
+    if (e->in_c > 4) return e->fail(strf("8-bit input: at most 4 channels (engine input has %d)", e->in_c));
+    *img_bytes = (size_t)e->in_c * e->in_h * e->in_w;
+    if (record_bytes != 0 && record_bytes < *img_bytes)
+        return e->fail(strf("record_bytes %zu < %zu pixel bytes per image", record_bytes, *img_bytes));
+    if (!e->cuda_ok(cudaSetDevice(e->device), "cudaSetDevice")) return PTQ8_ERR_CUDA;
+    if (!e->d_input_u8[slot] && !e->dalloc(&e->d_input_u8[slot], (size_t)e->max_batch * *img_bytes, "alloc 8-bit input"))
+        return PTQ8_ERR_CUDA;
+    return PTQ8_OK;
+}
+
+// Copy of n images of img_bytes pixels, record_bytes apart at src (0: packed), into a packed slot.
+cudaError_t copy_records(uint8_t* dst, const uint8_t* src, int n, size_t img_bytes, size_t record_bytes,
+                         cudaMemcpyKind kind, cudaStream_t s) {
+    if (record_bytes == 0 || record_bytes == img_bytes)
+        return cudaMemcpyAsync(dst, src, (size_t)n * img_bytes, kind, s);
+    return cudaMemcpy2DAsync(dst, img_bytes, src, record_bytes, img_bytes, n, kind, s);
+}
+
+}  // namespace
+
+int ptq8_engine_forward_u8(ptq8_engine* e, const uint8_t* x_host, int n, size_t record_bytes, float* logits_host) {
+    try {
+        if (!e || !x_host || !logits_host) return PTQ8_ERR_INVALID;
+        size_t img = 0;
+        int rc = u8_prepare(e, n, record_bytes, 0, &img);
+        if (rc) return rc;
+        // a pipelined call's copy into the same slot may still be in flight
+        if (e->copy_stream && !e->cuda_ok(cudaStreamSynchronize(e->copy_stream), "copy stream")) return PTQ8_ERR_CUDA;
+        cudaGraphExec_t ge;
+        if ((rc = graph_for(e, n, &ge, 0, true)) != 0) return rc;
+        if (!e->cuda_ok(copy_records(e->d_input_u8[0], x_host, n, img, record_bytes, cudaMemcpyHostToDevice, e->stream),
+                        "H2D") ||
+            !e->cuda_ok(cudaGraphLaunch(ge, e->stream), "graph launch"))
+            return PTQ8_ERR_CUDA;
+        mark_input_read(e);
+        if (!e->cuda_ok(cudaMemcpyAsync(logits_host, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
+                                        cudaMemcpyDeviceToHost, e->stream),
+                        "D2H") ||
+            !e->cuda_ok(cudaStreamSynchronize(e->stream), "forward"))
+            return PTQ8_ERR_CUDA;
+        return ptq8_engine_check_device_error(e);
+    } catch (const std::exception& ex) {
+        return e ? e->fail(strf("forward_u8: %s", ex.what()), PTQ8_ERR_CUDA) : PTQ8_ERR_CUDA;
+    }
+}
+
+int ptq8_engine_forward_u8_async(ptq8_engine* e, const uint8_t* x_host, int n, size_t record_bytes,
+                                 float* logits_host) {
+    try {
+        if (!e || !x_host || !logits_host) return PTQ8_ERR_INVALID;
+        const int slot = e->async_slot;
+        size_t img = 0;
+        int rc = u8_prepare(e, n, record_bytes, slot, &img);
+        if (rc) return rc;
+        if ((rc = ensure_copy_stream(e)) != 0) return rc;
+        cudaGraphExec_t ge;
+        if ((rc = graph_for(e, n, &ge, slot, true)) != 0) return rc;
+        // slot index k's free event follows the last forward that read either input of slot k
+        if (!e->cuda_ok(cudaStreamWaitEvent(e->copy_stream, e->ev_free[slot], 0), "wait slot") ||
+            !e->cuda_ok(copy_records(e->d_input_u8[slot], x_host, n, img, record_bytes, cudaMemcpyHostToDevice,
+                                     e->copy_stream),
+                        "H2D") ||
+            !e->cuda_ok(cudaEventRecord(e->ev_staged[slot], e->copy_stream), "record staged") ||
+            !e->cuda_ok(cudaStreamWaitEvent(e->stream, e->ev_staged[slot], 0), "wait staged") ||
+            !e->cuda_ok(cudaGraphLaunch(ge, e->stream), "graph launch") ||
+            !e->cuda_ok(cudaEventRecord(e->ev_free[slot], e->stream), "record free") ||
+            !e->cuda_ok(cudaMemcpyAsync(logits_host, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
+                                        cudaMemcpyDeviceToHost, e->stream),
+                        "D2H"))
+            return PTQ8_ERR_CUDA;
+        e->async_slot ^= 1;
+        return PTQ8_OK;
+    } catch (const std::exception& ex) {
+        return e ? e->fail(strf("forward_u8_async: %s", ex.what()), PTQ8_ERR_CUDA) : PTQ8_ERR_CUDA;
+    }
+}
+
+int ptq8_engine_forward_device_u8(ptq8_engine* e, const uint8_t* x_dev, int n, size_t record_bytes,
+                                  float* logits_dev) {
+    try {
+        if (!e || !x_dev || !logits_dev) return PTQ8_ERR_INVALID;
+        size_t img = 0;
+        int rc = u8_prepare(e, n, record_bytes, 0, &img);
+        if (rc) return rc;
+        if (e->copy_stream && !e->cuda_ok(cudaStreamSynchronize(e->copy_stream), "copy stream")) return PTQ8_ERR_CUDA;
+        cudaGraphExec_t ge;
+        if ((rc = graph_for(e, n, &ge, 0, true)) != 0) return rc;
+        if (!e->cuda_ok(copy_records(e->d_input_u8[0], x_dev, n, img, record_bytes, cudaMemcpyDeviceToDevice, e->stream),
+                        "input copy") ||
+            !e->cuda_ok(cudaGraphLaunch(ge, e->stream), "graph launch"))
+            return PTQ8_ERR_CUDA;
+        mark_input_read(e);
+        if (logits_dev != e->d_logits &&
+            !e->cuda_ok(cudaMemcpyAsync(logits_dev, e->d_logits, (size_t)n * e->model->fc_out * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, e->stream),
+                        "logits copy"))
+            return PTQ8_ERR_CUDA;
+        return PTQ8_OK;
+    } catch (const std::exception& ex) {
+        return e ? e->fail(strf("forward_device_u8: %s", ex.what()), PTQ8_ERR_CUDA) : PTQ8_ERR_CUDA;
     }
 }
 

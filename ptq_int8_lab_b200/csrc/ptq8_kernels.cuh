@@ -514,6 +514,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// The same wait, naming the 16 registers of an earlier tmem_ld16 as read and written, so
+// that the compiler keeps every use of them after it (a load whose wait comes later than
+// the next instructions, issued ahead of the computation on the previous load).
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                   "+r"(v[15])
+                 :
+                 : "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major operand tile whose rows are
 // `cb` bytes long and stored with the matching TMA swizzle (cb = 32/64/128):
@@ -944,6 +955,10 @@ struct ConvGeom {
     int tiles_w, tiles_h;       // M tiles along W and H
     int KW, SH, SW, PH, PW;     // kernel width, strides, paddings
     int coord_off;              // 1 when the A tensor carries the one-pixel border
+    // positional sub-convs (mode 0, TW = TH = 1): a tile is one output position of TN
+    // images, and only the taps that read inside the IH x IW input are loaded and
+    // multiplied (the others would multiply padding code 0)
+    int pos_tiles, IH, IW;
     // mode 1 (stride 1, same-size output): tiles are 128 consecutive bordered positions
     int KH, Hp, Wp;             // kernel height, bordered map dims
     int blk_off;                // first block row relative to the tile's first row
@@ -984,6 +999,26 @@ struct ConvGeom {
     const uint8_t* w4;
     int w4_ld, w_rows, b_packed;
 };
+
+// Kernel rows [kh0, kh1) and columns [kw0, kw1) that M tile mt multiplies: all of them,
+// or (positional sub-convs) those of its output position that read inside the input.
+__device__ __forceinline__ void tile_taps(const ConvGeom& g, int mt, int& kh0, int& kh1, int& kw0, int& kw1) {
+    kh0 = 0;
+    kh1 = g.KH;
+    kw0 = 0;
+    kw1 = g.KW;
+    if (g.pos_tiles) {
+        const uint32_t rest = fdiv(static_cast<uint32_t>(mt), g.fd_tiles_w);
+        const uint32_t nb = fdiv(rest, g.fd_tiles_h);
+        const int ow = static_cast<int>(static_cast<uint32_t>(mt) - rest * g.fd_tiles_w.d);
+        const int oh = static_cast<int>(rest - nb * g.fd_tiles_h.d);
+        const int ih = oh * g.SH - g.PH, iw = ow * g.SW - g.PW;   // input row / column of kernel tap 0
+        kh0 = max(0, -ih);
+        kh1 = min(g.KH, g.IH - ih);
+        kw0 = max(0, -iw);
+        kw1 = min(g.KW, g.IW - iw);
+    }
+}
 
 // Sign-extended int8 codes of the 8 int4 codes in packed word x (low nibble first):
 // lo/hi = codes 8i+0..3 / 8i+4..7 as bytes.
@@ -1094,18 +1129,28 @@ __device__ __forceinline__ void epilogue_fast(const ConvGeom& g, const EpiParams
         tc_fence_after();
         const uint32_t trow = tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16);
         uint32_t wq[2][8];
+        // accumulators of half hh in v[hh & 1] (h_lo is even): the load of the next half is
+        // issued before this half's arithmetic and waited for after it, so its TMEM latency
+        // overlaps the computation
+        uint32_t v[2][16], vx[2][16];
+        __syncwarp();   // each lane left the accumulator wait on its own
+        tmem_ld16(trow + h_lo * 16, v[0]);
+        if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + h_lo * 16, vx[0]);
+        tmem_wait_ld(v[0]);
+        if (AUX) tmem_wait_ld(vx[0]);
 #pragma unroll
         for (int hh = 0; hh < HALVES; ++hh) {
             if (hh < h_lo || hh >= h_hi) continue;
-            uint32_t v[16], vx[16];
+            const int cur = hh & 1, nxt = cur ^ 1;
             __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the per-lane stores
-            tmem_ld16(trow + hh * 16, v);
-            if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + hh * 16, vx);
-            tmem_wait_ld();
-            if (!valid) continue;
+            if (hh + 1 < h_hi) {
+                tmem_ld16(trow + (hh + 1) * 16, v[nxt]);
+                if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + (hh + 1) * 16, vx[nxt]);
+            }
+            if (valid) {
             float y[16];
-            dequant16(v, cc.fb + hh * 16, act, y, check);
-            if (AUX) dequant16(vx, cc.aux_fb + hh * 16, e.aux_act, res, false);   // aux K <= 128
+            dequant16(v[cur], cc.fb + hh * 16, act, y, check);
+            if (AUX) dequant16(vx[cur], cc.aux_fb + hh * 16, e.aux_act, res, false);   // aux K <= 128
             if constexpr (RES) {
 #pragma unroll
                 for (int j = 0; j < 16; j += 2) {
@@ -1134,6 +1179,12 @@ __device__ __forceinline__ void epilogue_fast(const ConvGeom& g, const EpiParams
 #pragma unroll
                 for (int j = 0; j < 4; ++j) wq[o][(hh & 1) * 4 + j] = w4[j];
                 if (hh & 1) st_v8(reinterpret_cast<uint32_t*>(qrow[o] + (hh >> 1) * 32), wq[o]);
+            }
+            }
+            if (hh + 1 < h_hi) {
+                __syncwarp();
+                tmem_wait_ld(v[nxt]);
+                if (AUX) tmem_wait_ld(vx[nxt]);
             }
         }
         tc_fence_before();
@@ -1270,8 +1321,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 h0 = static_cast<int>(rest - nb * g.fd_tiles_h.d) * g.TH;
                 n0 = static_cast<int>(nb) * g.TN;
             }
-            int tap = 0, cc = 0;
-            for (int ka = 0; ka < n_a; ++ka) {
+            int kh0 = 0, kh1 = 1, kw0 = 0, kw1 = 1;
+            if (MODE == 0) tile_taps(g, mt, kh0, kh1, kw0, kw1);
+            const int na = MODE == 0 ? (kh1 - kh0) * (kw1 - kw0) * g.n_cchunks : n_a;
+            int ki = kh0, kj = kw0, cc = 0;
+            for (int ka = 0; ka < na; ++ka) {
                 if (!mbar_wait_warp(empty0 + 8 * s, ph ^ 1, g.wait_limit)) {
                     if (lane == 0) atomicExch(g.err, ERR_WAIT_EMPTY);
                     ok = false;
@@ -1290,17 +1344,20 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     if (MODE == 1) {
                         tma_load_2d(smem_u32(sA + s * g.a_stage), &map_a, fb, ka * CB, mt * 128 + g.blk_off);
                     } else {
-                        const int ki = tap / g.KW;
-                        const int kj = tap - ki * g.KW;
                         tma_load_4d(smem_u32(sA + s * g.a_stage), &map_a, fb, cc * CB,
                                     w0 * g.SW + kj - g.PW + g.coord_off, h0 * g.SH + ki - g.PH + g.coord_off, n0);
-                        if (!g.b_resident) tma_load_2d(smem_u32(sB + s * sb_stride), &map_b, fb, ka * CB, nt * BN);
+                        if (!g.b_resident)
+                            tma_load_2d(smem_u32(sB + s * sb_stride), &map_b, fb,
+                                        ((ki * g.KW + kj) * g.n_cchunks + cc) * CB, nt * BN);
                     }
                 }
                 __syncwarp();
                 last_ph = (last_ph & ~(1u << s)) | (ph << s);
                 used |= 1u << s;
-                if (++cc == g.n_cchunks) { cc = 0; ++tap; }
+                if (++cc == g.n_cchunks) {
+                    cc = 0;
+                    if (++kj == kw1) { kj = kw0; ++ki; }
+                }
                 if (++s == S) { s = 0; ph ^= 1; }
             }
         }
@@ -1337,7 +1394,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
             tc_fence_after();
             const uint32_t d = tmem + static_cast<uint32_t>(buf * g.acc_cols);
-            for (int ka = 0; ka < n_a; ++ka) {
+            int kh0 = 0, kh1 = 1, kw0 = 0, kw1 = 1;
+            if (MODE == 0) tile_taps(g, mt, kh0, kh1, kw0, kw1);
+            const int na = MODE == 0 ? (kh1 - kh0) * (kw1 - kw0) * g.n_cchunks : n_a;
+            int ki = kh0, kj = kw0, cc = 0;   // mode 0: the K chunk's tap and channel chunk
+            for (int ka = 0; ka < na; ++ka) {
                 if (!mbar_wait_warp(full0 + 8 * s, ph, g.wait_limit)) {
                     if (lane == 0) atomicExch(g.err, ERR_WAIT_FULL);
                     ok = false;
@@ -1356,8 +1417,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                                            static_cast<uint32_t>(a_row_step), static_cast<uint32_t>(b_tap_step), idesc,
                                            ka != 0 ? 1u : 0u);
                 } else {
-                    const uint64_t db = bdesc0 + static_cast<uint64_t>(g.b_resident ? ka : s) * b_chunk_step;
+                    const int bc = (ki * g.KW + kj) * g.n_cchunks + cc;   // the chunk's index in the slab
+                    const uint64_t db = bdesc0 + static_cast<uint64_t>(g.b_resident ? bc : s) * b_chunk_step;
                     mma_chunk_elect<CB / 32>(d, da0, db, idesc, ka != 0 ? 1u : 0u);
+                    if (++cc == g.n_cchunks) {
+                        cc = 0;
+                        if (++kj == kw1) { kj = kw0; ++ki; }
+                    }
                 }
                 if (AUX && ka == 0) {
                     const uint32_t dx = d + static_cast<uint32_t>(g.aux_col);
@@ -1645,7 +1711,27 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 
 // ------------------------------------------------------------------ stem im2col
 
-// x: fp32 NCHW [N][C][H][W]; out: int8 rows of a bordered [N][OH+2][OW+2][kpad]
+// Normalisation of 8-bit pixels (CIFAR-10 records) into the network's fp32 input, in
+// the float32 operations of one of the reference's two input paths (per channel c,
+// px the pixel as a float, m[c] = mean*255 and d[c] as below, all float32):
+//   kNormDiv: x = (px - m) / d, d = std*255        (06-gpu-int8/cpp/ref_e2e.py:261-276)
+//   kNormMul: x = ((px / 255) * 255 - m) * d,
+//             d = 1 / (std*255)                      (06-gpu-int8/cpp/main.cpp:245-261)
+// each operation rounded to nearest (no contraction), as numpy and the reference's
+// host loop compute them.
+enum { kNormDiv = 0, kNormMul = 1 };
+struct U8Norm {
+    int mode;
+    float m[4], d[4];
+};
+__device__ __forceinline__ float normalize_px(uint32_t px, int c, const U8Norm& nm) {
+    const float v = static_cast<float>(px);
+    if (nm.mode == kNormMul) return __fmul_rn(__fsub_rn(__fmul_rn(__fdiv_rn(v, 255.0f), 255.0f), nm.m[c]), nm.d[c]);
+    return __fdiv_rn(__fsub_rn(v, nm.m[c]), nm.d[c]);
+}
+
+// x: fp32 NCHW [N][C][H][W] (U8: 8-bit pixels [N][C][H][W], normalised as above);
+// out: int8 rows of a bordered [N][OH+2][OW+2][kpad]
 // map (border rows are never written and stay zero) with k = (i*KW + j)*C + c,
 // codes of the stem's scale, zero for out-of-image taps and k >= KH*KW*C.
 // One CTA per band of `rows` output rows of one image.  The input band is read
@@ -1654,12 +1740,17 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 // table maps k to its offset in the band; then
 // each thread assembles the kpad-byte im2col row of one output pixel and writes
 // it with 16-byte stores (consecutive pixels: consecutive rows).
-__global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restrict__ out, int N, int C, int H,
+// U8: a pixel's code depends only on (channel, value), so the CTA first fills a
+// [C][256] code table (normalise + exact quantize of every value) and the band is
+// then a byte gather from it: the decode, normalisation and quantization of the
+// network input happen here, and the host sends 1 byte per input value instead of 4.
+template <bool U8>
+__global__ void stem_im2col_kernel(const void* __restrict__ xin, int8_t* __restrict__ out, int N, int C, int H,
                                    int W, int OH, int OW, int KH, int KW, int SH, int SW, int PH, int PW,
-                                   int kpad, int rows, float inv, double s) {
+                                   int kpad, int rows, float inv, double s, U8Norm nm) {
     griddep_launch();
-    griddep_wait();
-    extern __shared__ __align__(16) int8_t band[];   // [C][band_h][band_w], then int koff[kpad]
+    // [C][band_h][band_w], then int koff[kpad], then (U8) int8 lut[C][256]
+    extern __shared__ __align__(16) int8_t band[];
     const int bands = (OH + rows - 1) / rows;
     const int n = blockIdx.x / bands;
     const int r0 = (blockIdx.x - n * bands) * rows;
@@ -1668,6 +1759,12 @@ __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restri
     const int band_w = (OW - 1) * SW + KW;
     const int band_bytes = C * band_h * band_w;
     int* koff = reinterpret_cast<int*>(band + ((band_bytes + 15) & ~15));
+    int8_t* lut = reinterpret_cast<int8_t*>(koff + kpad);
+    if (U8) {   // depends on nothing an earlier kernel writes: built before the dependency wait
+        for (int i = threadIdx.x; i < C * 256; i += blockDim.x)
+            lut[i] = static_cast<int8_t>(sat8(quant_code(normalize_px(i & 255, i >> 8, nm), inv, s)));
+    }
+    griddep_wait();
     const int K = KH * KW * C;
     for (int k = threadIdx.x; k < kpad; k += blockDim.x) {
         int o = -1;
@@ -1682,23 +1779,45 @@ __global__ void stem_im2col_kernel(const float* __restrict__ x, int8_t* __restri
     // waits for one memory latency (a warp per band row, row after row, waited for one
     // per row).  Out-of-image elements are the zero padding.
     const int ih0 = r0 * SH - PH, iw0 = -PW;
-    const float* xn = x + static_cast<size_t>(n) * C * H * W;
     constexpr int kRound = 16;
-    for (int e0 = 0; e0 < band_bytes; e0 += kRound * static_cast<int>(blockDim.x)) {
-        float v[kRound];
+    if (!U8) {
+        const float* xn = static_cast<const float*>(xin) + static_cast<size_t>(n) * C * H * W;
+        for (int e0 = 0; e0 < band_bytes; e0 += kRound * static_cast<int>(blockDim.x)) {
+            float v[kRound];
 #pragma unroll
-        for (int m = 0; m < kRound; ++m) {
-            const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
-            const int rr = e / band_w, bw = e - rr * band_w;
-            const int c = rr / band_h, bh = rr - c * band_h;
-            const int ih = ih0 + bh, iw = iw0 + bw;
-            const bool in = e < band_bytes && ih >= 0 && ih < H && iw >= 0 && iw < W;
-            v[m] = in ? __ldg(xn + (static_cast<size_t>(c) * H + ih) * W + iw) : 0.0f;
+            for (int m = 0; m < kRound; ++m) {
+                const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+                const int rr = e / band_w, bw = e - rr * band_w;
+                const int c = rr / band_h, bh = rr - c * band_h;
+                const int ih = ih0 + bh, iw = iw0 + bw;
+                const bool in = e < band_bytes && ih >= 0 && ih < H && iw >= 0 && iw < W;
+                v[m] = in ? __ldg(xn + (static_cast<size_t>(c) * H + ih) * W + iw) : 0.0f;
+            }
+#pragma unroll
+            for (int m = 0; m < kRound; ++m) {
+                const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+                if (e < band_bytes) band[e] = static_cast<int8_t>(sat8(quant_code(v[m], inv, s)));
+            }
         }
+    } else {
+        const uint8_t* xn = static_cast<const uint8_t*>(xin) + static_cast<size_t>(n) * C * H * W;
+        __syncthreads();   // the code table
+        for (int e0 = 0; e0 < band_bytes; e0 += kRound * static_cast<int>(blockDim.x)) {
+            int v[kRound];   // lut index, or -1 for the zero padding
 #pragma unroll
-        for (int m = 0; m < kRound; ++m) {
-            const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
-            if (e < band_bytes) band[e] = static_cast<int8_t>(sat8(quant_code(v[m], inv, s)));
+            for (int m = 0; m < kRound; ++m) {
+                const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+                const int rr = e / band_w, bw = e - rr * band_w;
+                const int c = rr / band_h, bh = rr - c * band_h;
+                const int ih = ih0 + bh, iw = iw0 + bw;
+                const bool in = e < band_bytes && ih >= 0 && ih < H && iw >= 0 && iw < W;
+                v[m] = in ? (c << 8) + __ldg(xn + (static_cast<size_t>(c) * H + ih) * W + iw) : -1;
+            }
+#pragma unroll
+            for (int m = 0; m < kRound; ++m) {
+                const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+                if (e < band_bytes) band[e] = v[m] >= 0 ? lut[v[m]] : static_cast<int8_t>(0);
+            }
         }
     }
     __syncthreads();

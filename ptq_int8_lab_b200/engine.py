@@ -30,8 +30,12 @@ _lib = None
 
 PASS_CENTER_TAP = 1
 PASS_DECOMPOSE = 2
+PASS_POSITIONAL = 4
+PASS_ALL = PASS_CENTER_TAP | PASS_DECOMPOSE | PASS_POSITIONAL
 ACT_ABSMAX = 0
 ACT_MINMAX = 1
+NORM_DIV = 0   # 8-bit input: (px - mean*255) / (std*255)          (ref_e2e.py:272-274)
+NORM_MUL = 1   # 8-bit input: ((px/255)*255 - mean*255) * (1/(std*255))  (main.cpp:245-261)
 
 # every symbol include/ptq8.h declares
 EXPORTS = (
@@ -41,7 +45,9 @@ EXPORTS = (
     "ptq8_engine_create", "ptq8_engine_destroy", "ptq8_engine_last_error", "ptq8_engine_build",
     "ptq8_engine_set_act_mode", "ptq8_engine_set_calib", "ptq8_engine_set_input_shape",
     "ptq8_engine_alloc_scratch", "ptq8_engine_set_stream", "ptq8_engine_set_max_ctas", "ptq8_engine_stream", "ptq8_engine_forward",
-    "ptq8_engine_forward_device", "ptq8_engine_forward_async", "ptq8_engine_input_buffer", "ptq8_engine_logits_buffer", "ptq8_engine_run", "ptq8_engine_copy_logits",
+    "ptq8_engine_forward_device", "ptq8_engine_forward_async",
+    "ptq8_engine_set_input_norm", "ptq8_engine_forward_u8", "ptq8_engine_forward_u8_async",
+    "ptq8_engine_forward_device_u8", "ptq8_engine_input_buffer", "ptq8_engine_logits_buffer", "ptq8_engine_run", "ptq8_engine_copy_logits",
     "ptq8_engine_sync", "ptq8_engine_check_device_error", "ptq8_engine_set_wait_test", "ptq8_engine_tensor_info",
     "ptq8_engine_dump", "ptq8_engine_dump_range",
     "ptq8_engine_n_launches", "ptq8_engine_weight_bytes", "ptq8_engine_passes_log", "ptq8_engine_profile",
@@ -106,6 +112,10 @@ def lib() -> ctypes.CDLL:
         "ptq8_engine_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
         "ptq8_engine_forward_device": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
         "ptq8_engine_forward_async": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+        "ptq8_engine_set_input_norm": (c_int, [c_void_p, c_int, P(ctypes.c_float), P(ctypes.c_float)]),
+        "ptq8_engine_forward_u8": (c_int, [c_void_p, c_void_p, c_int, c_size, c_void_p]),
+        "ptq8_engine_forward_u8_async": (c_int, [c_void_p, c_void_p, c_int, c_size, c_void_p]),
+        "ptq8_engine_forward_device_u8": (c_int, [c_void_p, c_void_p, c_int, c_size, c_void_p]),
         "ptq8_engine_input_buffer": (c_void_p, [c_void_p]),
         "ptq8_engine_logits_buffer": (c_void_p, [c_void_p]),
         "ptq8_engine_run": (c_int, [c_void_p, c_int, c_int]),
@@ -331,6 +341,40 @@ class Int8Engine:
 
     def forward_device(self, x_ptr: int, n: int, logits_ptr: int):
         self._check(lib().ptq8_engine_forward_device(self._h, ctypes.c_void_p(x_ptr), n, ctypes.c_void_p(logits_ptr)))
+
+    def set_input_norm(self, mode: int = NORM_DIV, mean=None, std=None):
+        """Normalisation of 8-bit input (NORM_DIV / NORM_MUL; mean/std per channel, or
+        None for the CIFAR-10 constants)."""
+        if (mean is None) != (std is None):
+            raise Ptq8Error("mean and std: both given or both None")
+        if mean is None:
+            self._check(lib().ptq8_engine_set_input_norm(self._h, mode, None, None))
+            return
+        m = np.ascontiguousarray(mean, dtype=np.float32)
+        sd = np.ascontiguousarray(std, dtype=np.float32)
+        self._check(lib().ptq8_engine_set_input_norm(self._h, mode, _fptr(m), _fptr(sd)))
+
+    def forward_u8(self, x: np.ndarray, n: int = 0, record_bytes: int = 0, img_bytes: int = 3072) -> np.ndarray:
+        """8-bit pixels in, host fp32 logits out; synchronous.  x: uint8 [n][c][h][w]
+        (record_bytes 0), or a byte array whose first byte is image 0's first pixel, with
+        image i at i * record_bytes (e.g. a raw CIFAR-10 batch file from its second byte)."""
+        x = np.ascontiguousarray(x, dtype=np.uint8)
+        if record_bytes == 0:
+            n = x.shape[0]
+        elif n <= 0 or x.size < (n - 1) * record_bytes + img_bytes:
+            raise Ptq8Error(f"{n} records of {record_bytes} bytes do not fit in {x.size} bytes")
+        out = np.empty((n, self.model.fc_out), dtype=np.float32)
+        self._check(lib().ptq8_engine_forward_u8(self._h, x.ctypes.data, n, record_bytes, out.ctypes.data))
+        return out
+
+    def forward_u8_async(self, x_ptr: int, n: int, record_bytes: int, out_ptr: int):
+        """Pipelined 8-bit forward on raw (pinned) host pointers; sync() waits."""
+        self._check(lib().ptq8_engine_forward_u8_async(self._h, ctypes.c_void_p(x_ptr), n, record_bytes,
+                                                       ctypes.c_void_p(out_ptr)))
+
+    def forward_device_u8(self, x_ptr: int, n: int, record_bytes: int, logits_ptr: int):
+        self._check(lib().ptq8_engine_forward_device_u8(self._h, ctypes.c_void_p(x_ptr), n, record_bytes,
+                                                        ctypes.c_void_p(logits_ptr)))
 
     def input_buffer(self) -> int:
         return lib().ptq8_engine_input_buffer(self._h) or 0

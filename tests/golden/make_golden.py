@@ -17,6 +17,8 @@ script:
 * ``e2e_mv2_tiny/``     - a narrow MobileNetV2 exported by the reference's PTQ2
   exporter, its PTQC, and the forward composed from ``ref_int8.conv2d_int8``
   in ``topoblocks.replay_blocks`` order.
+* ``u8_norm.npz``       - raw CIFAR-10-format records (every pixel value in every
+  channel) and ``ref_e2e.read_test_batch``'s normalised fp32 input for them.
 * ``modelgen_sha.json`` - SHA-256 of the PTQ2 / PTQC files the reference's
   own producer code (03 fold_all_bn + calib, 09 build_blocks/export) writes for
   benchmark configs 0 and 2, to pin ``ptq_int8_lab_b200.modelgen``.
@@ -315,13 +317,39 @@ def make_modelgen_pin():
     (OUT / "modelgen_sha.json").write_text(json.dumps(res, indent=2))
 
 
+# --------------------------------------------------------------------------- 8-bit input
+
+def make_u8_norm():
+    """Raw CIFAR-10 records (1 label byte + 3072 pixel bytes) through the reference's
+    decode + normalisation (ref_e2e.read_test_batch)."""
+    import ref_e2e
+    rng = np.random.default_rng(5)
+    n = 3
+    px = np.empty((n, 3, 32, 32), np.uint8)
+    px[0] = (np.arange(3 * 1024) % 256).reshape(3, 32, 32)          # every value, every channel
+    px[1] = (255 - np.arange(3 * 1024) % 256).reshape(3, 32, 32)
+    px[2] = rng.integers(0, 256, size=(3, 32, 32), dtype=np.uint8)
+    labels = np.array([3, 7, 9], np.uint8)
+    rec = np.concatenate([labels[:, None], px.reshape(n, -1)], axis=1)
+    tmp = OUT / "_u8.raw"
+    tmp.write_bytes(rec.tobytes())
+    try:
+        x, lab = ref_e2e.read_test_batch(str(tmp), n)
+    finally:
+        tmp.unlink()
+    assert lab.tolist() == labels.tolist()
+    np.savez_compressed(OUT / "u8_norm.npz", records=rec.reshape(-1), x=np.asarray(x, np.float32))
+
+
+STEPS = {"kats": make_kats, "r18": make_r18_tiny, "mv2": make_mv2_tiny, "modelgen": make_modelgen_pin,
+         "u8": make_u8_norm}
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: python tests/golden/make_golden.py /path/to/ptq-int8-lab")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/ptq-int8-lab [step ...]  "
+                 f"(steps: {' '.join(STEPS)}; default all)")
     ref = Path(sys.argv[1])
     setup(ref)
-    make_kats()
-    make_r18_tiny()
-    make_mv2_tiny()
-    make_modelgen_pin()
+    for name in sys.argv[2:] or list(STEPS):
+        STEPS[name]()
     print("golden fixtures written to", OUT)

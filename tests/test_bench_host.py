@@ -14,7 +14,7 @@ def test_config_info_matches_configs():
         else:
             assert info["metric"] == bench.METRIC and info["name"].startswith("resnet18_" + c["stem"])
         assert ("mixed" in info["name"]) == bool(c.get("mixed"))
-        assert info["passes"] == (3 if c.get("passes") else 0)
+        assert info["passes"] == (7 if c.get("passes") else 0)
     assert bench.config_info(4)["batch"] == 8192   # the headline workload
 
 

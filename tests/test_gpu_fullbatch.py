@@ -49,13 +49,16 @@ def test_config_at_bench_batch(make_model, cfg):
 
 
 def test_config1_one_call_with_passes(make_model):
-    """Config 1 through the one-call interface (ptq8_load with both graph passes) at batch
-    1024.  On the CIFAR-stem graph the passes decline, so its codes are config 0's."""
+    """Config 1 through the one-call interface (ptq8_load with every graph pass) at batch
+    1024.  On the CIFAR-stem graph the center-tap and 2x2 + DepthToSpace rewrites decline;
+    the generalised positional pass runs the 8x8 / 4x4 convs as per-position sub-convs.
+    Its codes must be config 0's, bit for bit."""
     from ptq_int8_lab_b200 import engine as E
     from ptq_int8_lab_b200 import modelgen as mg
     paths = make_model(1)
     batch = mg.CONFIGS[1]["batch"]
-    eng = E.load_one_call(paths["model"], paths["calib"], paths["plan"], max_batch=batch,
-                          passes=E.PASS_CENTER_TAP | E.PASS_DECOMPOSE)
-    assert all(l.endswith("unchanged") for l in eng.passes_log().splitlines() if l)
+    eng = E.load_one_call(paths["model"], paths["calib"], paths["plan"], max_batch=batch, passes=E.PASS_ALL)
+    log = [l for l in eng.passes_log().splitlines() if l]
+    assert sum("positional" in l for l in log) == 8, log
+    assert all(l.endswith("unchanged") for l in log if "positional" not in l)
     _check(eng, paths, batch, seed=101)

@@ -221,3 +221,20 @@ def test_ptq8_load_plan_matches_python_reader(make_model):
 def test_model_load_rejects_directory(tmp_path):
     with pytest.raises(E.Ptq8Error, match="not a regular file"):
         E.Model.load(tmp_path)
+
+
+def test_u8_input_argument_checks(make_model):
+    """8-bit input entry points reject bad arguments on the host (no GPU work needed)."""
+    p = make_model(0)
+    eng = E.Int8Engine(0)
+    m = E.Model.load(p["model"])
+    eng.build(m, 8, 8)
+    L = E.lib()
+    assert L.ptq8_engine_set_input_norm(eng._h, 2, None, None) == 1
+    assert b"mode" in L.ptq8_engine_last_error(eng._h)
+    mean = np.array([0.5, 0.5, 0.5], np.float32)
+    bad = np.array([0.2, 0.0, 0.2], np.float32)
+    assert L.ptq8_engine_set_input_norm(eng._h, 0, E._fptr(mean), E._fptr(bad)) == 1
+    assert b"std" in L.ptq8_engine_last_error(eng._h)
+    assert L.ptq8_engine_set_input_norm(eng._h, 0, E._fptr(mean), None) == 1
+    assert L.ptq8_engine_forward_u8(eng._h, None, 4, 0, None) == 1

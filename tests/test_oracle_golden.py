@@ -119,3 +119,25 @@ def test_modelgen_matches_reference_producer(tmp_path, cfg):
     r = mg.make_config(int(cfg), tmp_path)
     assert mg.sha256(r["model"]) == want["ptq2_sha256"]
     assert mg.sha256(r["calib"]) == want["ptqc_sha256"]
+
+
+def test_u8_normalisation_matches_reference():
+    """normalize_u8 mode 0 against ref_e2e.read_test_batch on raw CIFAR-10 records
+    (tests/golden/u8_norm.npz): bit for bit."""
+    d = np.load(G / "u8_norm.npz")
+    rec = d["records"].reshape(-1, 3073)
+    px = rec[:, 1:].reshape(-1, 3, 32, 32)
+    got = O.normalize_u8(px, 0)
+    assert got.dtype == np.float32 and np.array_equal(got.view(np.uint32), d["x"].view(np.uint32))
+
+
+def test_u8_normalisation_mul_form():
+    """Mode 1 restates main.cpp:245-261 step by step in float32; the two forms differ by at
+    most a few ulps and agree on most values."""
+    px = (np.arange(3 * 256) % 256).astype(np.uint8).reshape(1, 3, 16, 16)
+    a, b = O.normalize_u8(px, 0), O.normalize_u8(px, 1)
+    p = np.float32(px[0, 1, 3, 7])
+    m = np.float32(0.4822) * np.float32(255.0)
+    inv = np.float32(1.0) / (np.float32(0.2435) * np.float32(255.0))
+    assert b[0, 1, 3, 7] == ((p / np.float32(255.0)) * np.float32(255.0) - m) * inv
+    assert np.max(np.abs(a - b) / np.maximum(np.abs(a), 1e-3)) < 1e-6
