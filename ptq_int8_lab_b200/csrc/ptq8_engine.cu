@@ -766,23 +766,21 @@ template <int CBI, int MODE>
 void fill_nout() { fill_res<CBI, MODE, 0>(); fill_res<CBI, MODE, 1>(); fill_res<CBI, MODE, 2>(); }
 template <int CBI>
 void fill_mode() { fill_nout<CBI, 0>(); fill_nout<CBI, 1>(); }
-// The same compile-time N tile epilogue for the 64-channel residual convs of the halo-block
-// pipeline: [code outputs 1/2][residual load][fp32 output][aux GEMM identity].
-void* g_conv_fast_res_table[2][2][2][2];
-template <int NOUT, int RES, int F32, int AUX>
+// The same compile-time N tile epilogue for 64-channel residual convs of the halo-block
+// pipeline whose residual is loaded and whose outputs are codes only: [code outputs 1/2].
+// (Measured at batch 8192: layer1.1.conv2 0.913 -> 0.889 ms against the column-stationary
+// epilogue; with an fp32 output and the aux-GEMM identity, layer1.0.conv2, it was slower,
+// 0.78 -> 1.05 ms, and keeps the column-stationary epilogue.)
+void* g_conv_fast_res_table[2];
+template <int NOUT>
 void fill_fast_res() {
-    g_conv_fast_res_table[NOUT - 1][RES][F32][AUX] =
-        reinterpret_cast<void*>(&conv_tc_kernel<64, 1, NOUT, (RES != 0 || AUX != 0), F32 != 0, AUX != 0, 64>);
+    g_conv_fast_res_table[NOUT - 1] = reinterpret_cast<void*>(&conv_tc_kernel<64, 1, NOUT, true, false, false, 64>);
 }
-// Whether the 64-channel residual convs use that epilogue (grouped warps, unrolled
-// 64-column rows) instead of the column-stationary one.
-constexpr bool kFastResidual = false;
 
 void fill_table() {
     static bool done = false;
     if (done) return;
-    fill_fast_res<1, 1, 0, 0>(); fill_fast_res<2, 1, 0, 0>(); fill_fast_res<1, 1, 1, 0>(); fill_fast_res<2, 1, 1, 0>();
-    fill_fast_res<1, 0, 1, 1>(); fill_fast_res<2, 0, 1, 1>(); fill_fast_res<1, 0, 0, 1>(); fill_fast_res<2, 0, 0, 1>();
+    fill_fast_res<1>(); fill_fast_res<2>();
     fill_mode<0>();
     fill_mode<1>();
     fill_mode<2>();
@@ -1160,12 +1158,12 @@ int finalize(ptq8_engine* e, int max_batch) {
             st.fast = (st.kind == K_TC || st.kind == K_STEM_IM2COL) && st.mode == 1 && st.n_ntiles == 1 &&
                       e->q[st.conv].view_oh == 0 && st.oc == st.bn && fast_index(st.cb, st.bn) >= 0 &&
                       nout >= 1 && nout <= 2 && !res && !f32 && st.aux_src < 0;
-            const bool fast_res = kFastResidual && !st.fast && st.kind == K_TC && st.mode == 1 && st.n_ntiles == 1 &&
+            const bool fast_res = !st.fast && st.kind == K_TC && st.mode == 1 && st.n_ntiles == 1 &&
                                   e->q[st.conv].view_oh == 0 && st.oc == 64 && st.bn == 64 && st.cb == 64 &&
-                                  nout >= 1 && nout <= 2 && (res || f32 || st.aux_src >= 0);
+                                  nout >= 1 && nout <= 2 && res && !f32 && st.aux_src < 0;
             if (fast_res) {
                 st.fast = true;
-                st.kfn = g_conv_fast_res_table[nout - 1][st.aux_src >= 0 ? 0 : res][f32][st.aux_src >= 0 ? 1 : 0];
+                st.kfn = g_conv_fast_res_table[nout - 1];
             } else if (st.fast) {
                 st.kfn = g_conv_fast_table[fast_index(st.cb, st.bn)][nout - 1];
             } else if (st.aux_src >= 0) {

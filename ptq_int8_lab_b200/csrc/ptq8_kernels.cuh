@@ -517,6 +517,19 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // The same wait, naming the 16 registers of an earlier tmem_ld16 as read and written, so
 // that the compiler keeps every use of them after it (a load whose wait comes later than
 // the next instructions, issued ahead of the computation on the previous load).
+// Compiler-ordering pins for the software-pipelined TMEM loads (no instruction is
+// emitted): pin_after makes the computation on v start after the preceding asm
+// statements (the next half's load issue); pin_before makes the values w be computed
+// before the following asm statements (the wait for that load).
+__device__ __forceinline__ void pin_after(uint32_t (&v)[16]) {
+    asm volatile(""
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                   "+r"(v[15]));
+}
+__device__ __forceinline__ void pin_before(const uint32_t (&w)[4]) {
+    asm volatile("" ::"r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]));
+}
 __device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;"
                  : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
@@ -1146,6 +1159,8 @@ __device__ __forceinline__ void epilogue_fast(const ConvGeom& g, const EpiParams
             if (hh + 1 < h_hi) {
                 tmem_ld16(trow + (hh + 1) * 16, v[nxt]);
                 if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + (hh + 1) * 16, vx[nxt]);
+                pin_after(v[cur]);
+                if (AUX) pin_after(vx[cur]);
             }
             if (valid) {
             float y[16];
@@ -1176,6 +1191,7 @@ __device__ __forceinline__ void epilogue_fast(const ConvGeom& g, const EpiParams
                 if (!kept[o]) continue;
                 uint32_t w4[4];
                 quant16q<true>(y, qx[o], sq[o], w4);
+                pin_before(w4);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) wq[o][(hh & 1) * 4 + j] = w4[j];
                 if (hh & 1) st_v8(reinterpret_cast<uint32_t*>(qrow[o] + (hh >> 1) * 32), wq[o]);
