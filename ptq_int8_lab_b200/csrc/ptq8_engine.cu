@@ -1325,7 +1325,25 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
                    st.kh, st.kw, st.sh, st.sw, st.ph, st.pw, ep);
         return;
     }
-    if (st.kind == K_STEM_IM2COL) {
+    if (st.kind == K_STEM_IM2COL && e->q[st.conv].spec.cin == 3 && e->q[st.conv].spec.kh == 3 &&
+        e->q[st.conv].spec.kw == 3 && e->q[st.conv].spec.sh == 1 && e->q[st.conv].spec.sw == 1 &&
+        e->q[st.conv].spec.ph == 1 && e->q[st.conv].spec.pw == 1 && st.kpad == 32 && st.oh == st.ih &&
+        st.ow == st.iw) {
+        // the CIFAR stem: pixel-major band, whole images per CTA while the band stays within 24 KB
+        int rows = st.oh;
+        while (rows > 1 && (size_t)3 * (rows + 2) * (st.iw + 2) > 24 * 1024) rows = (rows + 1) / 2;
+        const int bands = (st.oh + rows - 1) / rows;
+        const size_t band_bytes = (size_t)3 * (rows + 2) * (st.iw + 2);
+        const size_t smem = ((band_bytes + 16 + 15) & ~(size_t)15) + (e->cur_input_u8 ? 3 * 256 : 0);
+        const FastDiv fbw = make_fastdiv((uint32_t)(st.iw + 2)), fbh = make_fastdiv((uint32_t)(rows + 2));
+        if (e->cur_input_u8)
+            launch_pdl(stem_im2col3_kernel<true>, dim3(n * bands), dim3(256), smem, s, (const void*)e->cur_input_u8,
+                       st.d_im2col, n, st.ih, st.iw, rows, fbw, fbh, (float)(1.0 / st.s_in), st.s_in, e->u8_norm);
+        else
+            launch_pdl(stem_im2col3_kernel<false>, dim3(n * bands), dim3(256), smem, s,
+                       (const void*)(e->cur_input ? e->cur_input : (const float*)e->d_input), st.d_im2col, n, st.ih,
+                       st.iw, rows, fbw, fbh, (float)(1.0 / st.s_in), st.s_in, e->u8_norm);
+    } else if (st.kind == K_STEM_IM2COL) {
         const ConvSpec& c = e->q[st.conv].spec;
         // whole images per CTA while the quantized band stays within 24 KB of shared memory
         const size_t band_w = (size_t)(st.ow - 1) * c.sw + c.kw;

@@ -1865,6 +1865,99 @@ __global__ void stem_im2col_kernel(const void* __restrict__ xin, int8_t* __restr
     }
 }
 
+// The CIFAR stem (3 channels, 3x3, stride 1, pad 1, 32-byte im2col rows), same output as
+// stem_im2col_kernel: the band is kept pixel-major, [band_h][band_w][3] codes, so the 27
+// codes of output pixel (h, w) -- k = (i*3 + j)*3 + c -- are three runs of 9 consecutive
+// bytes, one per kernel row i, starting at ((h + i)*band_w + w)*3.  Each run is read as three
+// aligned words and funnel-shifted into place (no per-byte loads), and the row goes out as two
+// 16-byte stores.  Band element indices are split by multiply-high division (fd_bw = band_w,
+// fd_bh = band_h).  U8: 8-bit pixels through the per-CTA code table, as in stem_im2col_kernel.
+template <bool U8>
+__global__ void stem_im2col3_kernel(const void* __restrict__ xin, int8_t* __restrict__ out, int N, int H, int W,
+                                    int rows, FastDiv fd_bw, FastDiv fd_bh, float inv, double s, U8Norm nm) {
+    griddep_launch();
+    // [band_h][band_w][3] codes, 16 spare bytes (the last run's word reads), then (U8) int8 lut[3][256]
+    extern __shared__ __align__(16) int8_t band[];
+    const int bands = (H + rows - 1) / rows;
+    const int n = blockIdx.x / bands;
+    const int r0 = (blockIdx.x - n * bands) * rows;
+    const int r1 = min(H, r0 + rows);
+    const int band_w = static_cast<int>(fd_bw.d), band_h = static_cast<int>(fd_bh.d);
+    const int band_bytes = band_h * band_w * 3;
+    int8_t* lut = band + ((band_bytes + 16 + 15) & ~15);
+    if (U8) {   // depends on nothing an earlier kernel writes: built before the dependency wait
+        for (int i = threadIdx.x; i < 3 * 256; i += blockDim.x)
+            lut[i] = static_cast<int8_t>(sat8(quant_code(normalize_px(i & 255, i >> 8, nm), inv, s)));
+    }
+    if (threadIdx.x < 16) band[band_bytes + threadIdx.x] = 0;
+    griddep_wait();
+    if (U8) __syncthreads();   // the code table
+    // band element e = (c * band_h + bh) * band_w + bw: consecutive threads read consecutive
+    // input columns; 16 loads in flight per thread; out-of-image elements are code 0
+    const int ih0 = r0 - 1;
+    constexpr int kRound = 16;
+    const size_t img = static_cast<size_t>(n) * 3 * H * W;
+    for (int e0 = 0; e0 < band_bytes; e0 += kRound * static_cast<int>(blockDim.x)) {
+        int dst[kRound];
+        float v[kRound];
+        int li[kRound];
+#pragma unroll
+        for (int m = 0; m < kRound; ++m) {
+            const int e = e0 + m * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+            const uint32_t rr = fdiv(static_cast<uint32_t>(e), fd_bw);
+            const int bw = e - static_cast<int>(rr) * band_w;
+            const uint32_t c = fdiv(rr, fd_bh);
+            const int bh = static_cast<int>(rr) - static_cast<int>(c) * band_h;
+            const int ih = ih0 + bh, iw = bw - 1;
+            const bool in = e < band_bytes && ih >= 0 && ih < H && iw >= 0 && iw < W;
+            const size_t gi = img + (static_cast<size_t>(c) * H + ih) * W + iw;
+            dst[m] = e < band_bytes ? (bh * band_w + bw) * 3 + static_cast<int>(c) : -1;
+            if (U8) {
+                li[m] = in ? static_cast<int>(c << 8) + __ldg(static_cast<const uint8_t*>(xin) + gi) : -1;
+            } else {
+                v[m] = in ? __ldg(static_cast<const float*>(xin) + gi) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < kRound; ++m) {
+            if (dst[m] < 0) continue;
+            if (U8) band[dst[m]] = li[m] >= 0 ? lut[li[m]] : static_cast<int8_t>(0);
+            else band[dst[m]] = static_cast<int8_t>(sat8(quant_code(v[m], inv, s)));
+        }
+    }
+    __syncthreads();
+    const int npix = (r1 - r0) * W;
+    int8_t* obase = out + ((static_cast<size_t>(n) * (H + 2) + r0 + 1) * (W + 2) + 1) * 32;
+    const uint32_t* bw32 = reinterpret_cast<const uint32_t*>(band);
+    for (int p = threadIdx.x; p < npix; p += blockDim.x) {
+        const int hl = p / W, w = p - (p / W) * W;
+        uint32_t s0[3], s1[3], b8[3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const int off = ((hl + i) * band_w + w) * 3;
+            const int a = off >> 2;
+            const uint32_t sh = static_cast<uint32_t>(off & 3) * 8u;
+            const uint32_t w0 = bw32[a], w1 = bw32[a + 1], w2 = bw32[a + 2];
+            s0[i] = __funnelshift_r(w0, w1, sh);   // bytes 0..3 of the run
+            s1[i] = __funnelshift_r(w1, w2, sh);   // bytes 4..7
+            b8[i] = (w2 >> sh) & 0xFFu;            // byte 8
+        }
+        // row bytes: run 0 at 0..8, run 1 at 9..17, run 2 at 18..26, zeros at 27..31
+        uint4 lo, hi;
+        lo.x = s0[0];
+        lo.y = s1[0];
+        lo.z = b8[0] | (s0[1] << 8);
+        lo.w = (s0[1] >> 24) | (s1[1] << 8);
+        hi.x = (s1[1] >> 24) | (b8[1] << 8) | (s0[2] << 16);
+        hi.y = (s0[2] >> 16) | (s1[2] << 16);
+        hi.z = (s1[2] >> 16) | (b8[2] << 16);
+        hi.w = 0u;
+        int8_t* o = obase + static_cast<size_t>(hl * (W + 2) + w) * 32;
+        st_v4(o, lo);
+        st_v4(o + 16, hi);
+    }
+}
+
 // ------------------------------------------------------------------ depthwise conv
 
 // Depthwise kxk conv over bordered int8 codes [N][H+2][W+2][ldi] (C channels),
