@@ -777,9 +777,18 @@ void fill_fast_res() {
     g_conv_fast_res_table[NOUT - 1] = reinterpret_cast<void*>(&conv_tc_kernel<64, 1, NOUT, true, false, false, 64>);
 }
 
+// Mode 2 (stride-2 3x3 convs over 64-byte pixels, pixel-pair boxes), codes-only outputs:
+// [code outputs 1/2].
+void* g_conv_pair_table[2];
+template <int NOUT>
+void fill_pair() {
+    g_conv_pair_table[NOUT - 1] = reinterpret_cast<void*>(&conv_tc_kernel<64, 2, NOUT, false, false, false>);
+}
+
 void fill_table() {
     static bool done = false;
     if (done) return;
+    fill_pair<1>(); fill_pair<2>();
     fill_fast_res<1>(); fill_fast_res<2>();
     fill_mode<0>();
     fill_mode<1>();
@@ -1021,6 +1030,20 @@ int finalize(ptq8_engine* e, int max_batch) {
                 if (!choose_pipeline(st, 2)) st.mode = 0;
             }
         }
+        // mode 2: a stride-2 3x3 conv over 64-byte pixels (64 channels) reads, per kernel row, one
+        // 4-D box of pixel pairs (2w, 2w+1) -- taps 0 and 1 in its two 64-byte halves -- and one of
+        // the pairs one further (tap 2 in the first half): 6 boxes of 128 rows x 128 bytes per tile
+        // instead of 9 of 64-byte rows, whose per-row cost bounds these convs.  Needs resident
+        // weights and a codes-only output.
+        if (st.kind == K_TC && st.mode == 0 && cq.view_oh == 0 && !cq.pos_tiles && st.kh == 3 && st.kw == 3 &&
+            st.sh == 2 && st.sw == 2 && st.ph == 1 && st.pw == 1 && cpad == 64 && st.cb == 64 &&
+            e->vals[st.in_val].ldq == 64 && (st.iw + 2) % 2 == 0 && st.aux_src < 0 && st.res_val < 0 &&
+            !e->vals[st.out_val].need_f32 && e->vals[st.out_val].scales.size() >= 1 &&
+            e->vals[st.out_val].scales.size() <= 2 && st.TW * st.TH * st.TN == 128) {
+            st.mode = 2;
+            st.a_stage = 128 * 128;
+            if (!choose_pipeline(st, 2) || !st.b_resident) st.mode = 0;
+        }
         if (st.kind == K_STEM_IM2COL) {
             // the stem GEMM reads its bordered im2col rows as a 1x1 conv: tiles of 128 consecutive
             // bordered rows, one 2-D box each (4-D boxes of 32-byte rows were several times slower)
@@ -1131,6 +1154,17 @@ int finalize(ptq8_engine* e, int max_batch) {
             const Value& vin = e->vals[st.in_val];
             int8_t* base = vin.codes[vin.code_index(st.s_in)];
             const cuuint64_t hp = vin.h + 2, wp = vin.w + 2;
+            if (st.mode == 2) {   // elements are pixel pairs: 128 bytes of two 64-byte code rows
+                cuuint64_t pdims[4] = {128, wp / 2, hp, (cuuint64_t)max_batch};
+                cuuint64_t pstrides[3] = {128, (cuuint64_t)vin.ldq * wp, (cuuint64_t)vin.ldq * wp * hp};
+                cuuint32_t pbox[4] = {128, (cuuint32_t)st.TW, (cuuint32_t)(st.TH * 2), (cuuint32_t)st.TN};
+                cuuint32_t pestr[4] = {1, 1, 2, 1};
+                if (pbox[2] > 256 || !make_map(e, &st.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, pdims, pstrides,
+                                                pbox, pestr, swizzle_for(128)))
+                    return pbox[2] > 256 ? e->fail(strf("conv[%d]: pair box taller than 256 rows", st.conv))
+                                         : PTQ8_ERR_CUDA;
+                continue;
+            }
             cuuint64_t dims[4] = {(cuuint64_t)vin.c, wp, hp, (cuuint64_t)max_batch};
             cuuint64_t strides[3] = {(cuuint64_t)vin.ldq, (cuuint64_t)vin.ldq * wp, (cuuint64_t)vin.ldq * wp * hp};
             cuuint32_t box[4] = {(cuuint32_t)st.cb, (cuuint32_t)(st.TW * st.sw), (cuuint32_t)(st.TH * st.sh),
@@ -1166,6 +1200,8 @@ int finalize(ptq8_engine* e, int max_batch) {
                 st.kfn = g_conv_fast_res_table[nout - 1];
             } else if (st.fast) {
                 st.kfn = g_conv_fast_table[fast_index(st.cb, st.bn)][nout - 1];
+            } else if (st.mode == 2) {
+                st.kfn = g_conv_pair_table[nout - 1];
             } else if (st.aux_src >= 0) {
                 if (nout < 1 || nout > 2) return e->fail(strf("conv[%d]: stem identity fusion needs 1-2 code outputs", st.conv));
                 st.kfn = g_conv_aux_table[cb_index(st.cb) - 1][nout - 1][f32];
@@ -1393,7 +1429,7 @@ void enqueue_step(ptq8_engine* e, int n, size_t si) {
         g.a_bytes = (uint32_t)(st.blk_rows * st.cb);
     } else {
         g.m_tiles = g.tiles_w * g.tiles_h * ((n + st.TN - 1) / st.TN);
-        g.a_bytes = (uint32_t)(st.TW * st.TH * st.TN * st.cb);
+        g.a_bytes = (uint32_t)(st.TW * st.TH * st.TN * (st.mode == 2 ? 128 : st.cb));
     }
     g.a_stage = st.a_stage;
     g.n_kchunks = st.n_kchunks;

@@ -961,7 +961,8 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t x, const FastDiv& f) {
 }
 
 struct ConvGeom {
-    int mode;                   // 0: per-tap 4-D tile loads; 1: one halo block per tile, taps = shifted views
+    int mode;                   // 0: per-tap 4-D tile loads; 1: one halo block per tile, taps = shifted views;
+                                // 2: stride-2 3x3 over 64-byte pixels, one 4-D box of pixel pairs per two taps
     int N, OH, OW;              // output map (per image)
     // mode 0
     int TW, TH, TN;             // one M tile = TN images x TH rows x TW cols (<= 128 positions)
@@ -1307,7 +1308,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     tc_fence_after();
     griddep_launch();
     const uint32_t tmem = tslot;
-    const int n_a = MODE == 1 ? g.n_cchunks : g.n_kchunks;   // A loads per tile
+    // A loads per tile (mode 2: a pair box and a single-tap box per kernel row)
+    const int n_a = MODE == 1 ? g.n_cchunks : (MODE == 2 ? 2 * g.KH : g.n_kchunks);
 
     if (warp == 0) {
         // ---------------- TMA producer (whole warp; one elected lane issues the copies)
@@ -1330,7 +1332,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         griddep_wait();   // A tiles (and the aux rows) are earlier kernels' outputs
         for (int mt = blockIdx.x; ok && mt < g.m_tiles; mt += gridDim.x) {
             int w0 = 0, h0 = 0, n0 = 0;
-            if (MODE == 0) {
+            if (MODE == 0 || MODE == 2) {
                 const uint32_t rest = fdiv(static_cast<uint32_t>(mt), g.fd_tiles_w);
                 const uint32_t nb = fdiv(rest, g.fd_tiles_h);
                 w0 = static_cast<int>(static_cast<uint32_t>(mt) - rest * g.fd_tiles_w.d) * g.TW;
@@ -1359,6 +1361,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     if (aux) tma_load_2d(smem_u32(sA + s * g.a_stage + g.aux_off), &map_xa, fb, 0, mt * 128);
                     if (MODE == 1) {
                         tma_load_2d(smem_u32(sA + s * g.a_stage), &map_a, fb, ka * CB, mt * 128 + g.blk_off);
+                    } else if (MODE == 2) {
+                        // kernel row ka / 2: the pixel pairs (2w, 2w+1) of bordered columns 2w, 2w+1 (taps
+                        // 0 and 1) for ka even, the pairs one further (tap 2 in their first half) for ka odd;
+                        // bordered input row 2h + kernel row (element stride 2)
+                        tma_load_4d(smem_u32(sA + s * g.a_stage), &map_a, fb, 0, w0 + (ka & 1), h0 * 2 + (ka >> 1), n0);
                     } else {
                         tma_load_4d(smem_u32(sA + s * g.a_stage), &map_a, fb, cc * CB,
                                     w0 * g.SW + kj - g.PW + g.coord_off, h0 * g.SH + ki - g.PH + g.coord_off, n0);
@@ -1389,7 +1396,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const uint32_t idesc = make_idesc_i8(BN);
         // descriptors of stage 0 / B chunk 0; other stages, taps and chunks only move the
         // start address (16-byte units), so the issue loop is register adds.
-        const uint64_t adesc0 = make_sdesc(smem_u32(sA), CB);
+        const uint64_t adesc0 = make_sdesc(smem_u32(sA), MODE == 2 ? 128 : CB);
         const uint64_t bdesc0 = make_sdesc(smem_u32(sB), CB);
         const uint64_t a_row_step = static_cast<uint64_t>((g.Wp * CB) >> 4);      // mode 1: next kernel row
         const uint64_t b_tap_step = static_cast<uint64_t>((g.n_cchunks * sb_stride) >> 4);
@@ -1422,7 +1429,15 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
                 tc_fence_after();
                 const uint64_t da0 = adesc0 + static_cast<uint64_t>(s) * a_stage_step;
-                if (MODE == 1 && g.KH == 1) {
+                if (MODE == 2) {
+                    // A: 128-byte rows (two taps' 64 channels, 128-byte swizzle); B: the 64-byte chunks of
+                    // taps 3i+j, resident.  Pair box: A bytes 0-63 x tap 3i, 64-127 x tap 3i+1; single-tap
+                    // box: A bytes 0-63 x tap 3i+2.
+                    const int t = 3 * (ka >> 1) + ((ka & 1) ? 2 : 0);
+                    const uint64_t db = bdesc0 + static_cast<uint64_t>(t) * b_chunk_step;
+                    mma_chunk_elect<2>(d, da0, db, idesc, ka != 0 ? 1u : 0u);
+                    if ((ka & 1) == 0) mma_chunk_elect<2>(d, da0 + 4, db + b_chunk_step, idesc, 1u);
+                } else if (MODE == 1 && g.KH == 1) {
                     // one tap (the stem GEMM over its bordered im2col rows): the block is the tile
                     mma_chunk_elect<CB / 32>(d, da0, bdesc0 + static_cast<uint64_t>(ka) * b_chunk_step, idesc,
                                              ka != 0 ? 1u : 0u);
