@@ -1143,21 +1143,31 @@ __device__ __forceinline__ void epilogue_fast(const ConvGeom& g, const EpiParams
         tc_fence_after();
         const uint32_t trow = tmem + static_cast<uint32_t>(buf * g.acc_cols) + (static_cast<uint32_t>(quad * 32) << 16);
         uint32_t wq[2][8];
-        // accumulators of half hh in v[hh & 1] (h_lo is even): the load of the next half is
-        // issued before this half's arithmetic and waited for after it, so its TMEM latency
-        // overlaps the computation
+        // accumulators of half hh in v[hh & 1] (h_lo is even).  Without a residual the load of
+        // the next half is issued before this half's arithmetic and waited for after it, so its
+        // TMEM latency overlaps the computation; with one, each half is loaded and waited for in
+        // turn (the second buffer pushed the residual kernels into spills: layer1.1.conv2 0.886 ms
+        // pipelined against 0.839 ms without)
         uint32_t v[2][16], vx[2][16];
-        __syncwarp();   // each lane left the accumulator wait on its own
-        tmem_ld16(trow + h_lo * 16, v[0]);
-        if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + h_lo * 16, vx[0]);
-        tmem_wait_ld(v[0]);
-        if (AUX) tmem_wait_ld(vx[0]);
+        constexpr bool kPipe = !RES;
+        if (kPipe) {
+            __syncwarp();   // each lane left the accumulator wait on its own
+            tmem_ld16(trow + h_lo * 16, v[0]);
+            if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + h_lo * 16, vx[0]);
+            tmem_wait_ld(v[0]);
+            if (AUX) tmem_wait_ld(vx[0]);
+        }
 #pragma unroll
         for (int hh = 0; hh < HALVES; ++hh) {
             if (hh < h_lo || hh >= h_hi) continue;
             const int cur = hh & 1, nxt = cur ^ 1;
             __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the per-lane stores
-            if (hh + 1 < h_hi) {
+            if (!kPipe) {
+                tmem_ld16(trow + hh * 16, v[cur]);
+                if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + hh * 16, vx[cur]);
+                tmem_wait_ld(v[cur]);
+                if (AUX) tmem_wait_ld(vx[cur]);
+            } else if (hh + 1 < h_hi) {
                 tmem_ld16(trow + (hh + 1) * 16, v[nxt]);
                 if (AUX) tmem_ld16(trow + static_cast<uint32_t>(g.aux_col) + (hh + 1) * 16, vx[nxt]);
                 pin_after(v[cur]);
@@ -1198,7 +1208,7 @@ __device__ __forceinline__ void epilogue_fast(const ConvGeom& g, const EpiParams
                 if (hh & 1) st_v8(reinterpret_cast<uint32_t*>(qrow[o] + (hh >> 1) * 32), wq[o]);
             }
             }
-            if (hh + 1 < h_hi) {
+            if (kPipe && hh + 1 < h_hi) {
                 __syncwarp();
                 tmem_wait_ld(v[nxt]);
                 if (AUX) tmem_wait_ld(vx[nxt]);
