@@ -854,10 +854,11 @@ int acc_cols_for(int bn) {
 int n_acc_for(int cols) { return std::min(8, 512 / cols); }
 int n_groups_for(int cols, int bn, bool res) {
     if (res && bn > 48 && bn <= 64) return 1;
-    // residual convs with 65..128-channel N tiles: two groups of 8 warps (two slices per lane
-    // quadrant), each double-buffering its accumulators (layer2.1.conv2 0.668 -> 0.642 ms at
-    // batch 8192 against four groups of 4 warps)
-    if (res && bn > 64 && bn <= 128) return std::min(2, n_acc_for(cols));
+    // 65..128-channel N tiles: two groups of 8 warps (two slices per lane quadrant), each
+    // double-buffering its accumulators, against four groups of 4 warps at batch 8192:
+    // layer2.1.conv2 0.668 -> 0.642 ms, layer2.1.conv1 0.286 -> 0.277 ms, layer2.0.conv1
+    // 0.248 -> 0.240 ms
+    if (bn > 64 && bn <= 128) return std::min(2, n_acc_for(cols));
     return std::min(4, n_acc_for(cols));
 }
 
